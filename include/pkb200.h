@@ -1,0 +1,158 @@
+/* pkb200.h - C ABI of libpkb200.so, the B200 (sm_100a) kernel library that
+ * replaces the reference's kernels/generated/*.cu launch entry points.
+ *
+ * Conventions shared by every entry point:
+ *   - bf16 tensors are raw 16-bit brain-float values (the reference's pk_bf16 /
+ *     __nv_bfloat16, kernels/template/kernel_common.h:42-60), row-major.
+ *   - The caller allocates and owns every device buffer; outputs are sized by
+ *     the caller. Inputs are not modified unless stated (the KV cache of the
+ *     append entry is written in place).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream),
+ *     as in the reference's launch_* functions. Launches are asynchronous.
+ *   - Return value: 0 on success, otherwise a cudaError_t value
+ *     (cudaErrorInvalidValue = 1 for a rejected shape/pointer). The reference's
+ *     void launch_* functions only print on error (kernel_common.h:160-167);
+ *     the C++ symbols below keep that behaviour and forward to these.
+ *
+ * The reference's own C++ entry points (mangled, pk_bf16 = __nv_bfloat16) are
+ * exported unchanged by the same library and declared at the bottom for C++
+ * callers (cuda_run_main.cpp:59-71 and bench_cuda.cpp:50-58 link against them).
+ */
+#ifndef PKB200_H
+#define PKB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library version string ("pkb200 <major>.<minor> sm_100a"). */
+const char* pkb200_version(void);
+
+/* y = bf16( x / sqrt(mean(x^2) + eps) [* weight] ) over the last axis.
+ * Replaces launch_rmsnorm (kernels/generated/rmsnorm.cu:106-108). weight may be NULL. */
+int pkb200_rmsnorm(const void* input, const void* weight, void* output, int rows, int cols,
+                   float eps, void* stream);
+
+/* Exact erf GELU over n elements. Replaces launch_gelu (gelu.cu:56). */
+int pkb200_gelu(const void* input, void* output, long long n, void* stream);
+
+/* C = bf16(A @ B); A [M,K], B [K,N]. Replaces launch_matmul (matmul.cu:78-79). */
+int pkb200_matmul(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
+
+/* C = fp32(A @ B) (no rounding): the partial sums a tensor-parallel rank feeds
+ * to the all-reduce. New; no reference counterpart (the reference has no TP). */
+int pkb200_matmul_f32out(const void* A, const void* B, float* C, int M, int N, int K,
+                         void* stream);
+
+/* C = bf16(rmsnorm(X; gamma, eps) @ W). gamma may be NULL (the reference kernel
+ * has no gamma: fused_rmsnorm_matmul.cu:110-112). Replaces
+ * launch_fused_rmsnorm_matmul (fused_rmsnorm_matmul.cu:114-116); the gamma
+ * argument follows golden.fused_rmsnorm_matmul (tests/golden/golden.py:96-100).
+ * Uses a library-owned device workspace of M*K bf16 for the normalised rows. */
+int pkb200_fused_rmsnorm_matmul(const void* X, const void* W, const void* gamma, void* out,
+                                int M, int N, int K, float eps, void* stream);
+
+/* out = bf16(gelu(bf16(bf16(A @ B) + bias))). Replaces launch_fused_matmul_bias_gelu
+ * (fused_matmul_bias_gelu.cu:104-106). */
+int pkb200_fused_matmul_bias_gelu(const void* A, const void* B, const void* bias, void* out,
+                                  int M, int N, int K, void* stream);
+
+/* out = bf16(bf16(bf16(A @ B) + bias) + resid); resid [M,N]. The MLP's second
+ * GEMM with the residual add (golden.add/bias, tests/golden/golden.py:48-55) in
+ * its epilogue; the reference has no kernel for this add. */
+int pkb200_matmul_bias_residual(const void* A, const void* B, const void* bias,
+                                const void* resid, void* out, int M, int N, int K, void* stream);
+
+/* out = bf16(bf16(bf16(Y) + bias) + resid) for an fp32 Y [M,N] (the all-reduced
+ * tensor-parallel partial sums). */
+int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
+                             int M, int N, void* stream);
+
+/* C = bf16(A @ (Wq * scale[n])); A bf16 [M,K], Wq int8 [K,N], scale fp32 [N].
+ * Replaces launch_matmul_int8 (kernels/generated/matmul_int8.cu:97-98). */
+int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void* C, int M,
+                       int N, int K, void* stream);
+
+/* Bytes of device workspace pkb200_mlp_block / pkb200_mlp_block_int8 need. */
+size_t pkb200_mlp_block_workspace_size(int M, int d, int ffn);
+
+/* Y = X + (GELU(rmsnorm(X;gamma,eps) @ W1 + b1) @ W2 + b2), every op rounded to
+ * bf16 as the golden composes it (golden.py:48-100; tests/e2e/conftest.py:104-107;
+ * examples/mlp_block.mlir semantics with the biases BASELINE adds).
+ * X,Y [M,d]; gamma [d]; W1 [d,ffn]; b1 [ffn]; W2 [ffn,d]; b2 [d].
+ * workspace: caller-owned device memory of pkb200_mlp_block_workspace_size bytes. */
+int pkb200_mlp_block(const void* X, const void* gamma, const void* W1, const void* b1,
+                     const void* W2, const void* b2, void* Y, int M, int d, int ffn, float eps,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same chain with int8 weight-only W1/W2 and fp32 per-output-channel scales
+ * (quant_golden.matmul_int8 semantics, tests/golden/quant_golden.py:91-101). */
+int pkb200_mlp_block_int8(const void* X, const void* gamma, const int8_t* W1q,
+                          const float* s1, const void* b1, const int8_t* W2q, const float* s2,
+                          const void* b2, void* Y, int M, int d, int ffn, float eps,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Causal (or full) scaled-dot-product prefill attention. Q/O [B,H,S_q,D],
+ * K/V [B,H,S_kv,D]. Row i sees keys j <= S_kv - S_q + i when causal != 0.
+ * Replaces launch_attention_prefill (kernels/generated/attention_prefill.cu:169-172). */
+int pkb200_attention_prefill(const void* Q, const void* K, const void* V, void* O, int B,
+                             int H, int S_q, int S_kv, int D, float scale, int causal,
+                             void* stream);
+
+/* out [B,H,S_cache+S_new,D] = concat(cache, new_rows) along the sequence axis
+ * (out-of-place). Replaces launch_kv_cache_update (kv_cache_update.cu:67-69). */
+int pkb200_kv_cache_update(const void* cache, const void* new_rows, void* out, int B, int H,
+                           int S_cache, int S_new, int D, void* stream);
+
+/* Fused KV append + prefill attention over a preallocated cache:
+ *   Kcache/Vcache [B,H,S_max,D] hold S_cache valid rows; K_new/V_new [B,H,S_q,D]
+ *   are written in place into rows [S_cache, S_cache+S_q) and Q attends to the
+ *   S_cache+S_q keys (golden.fused_kv_append_attention, golden.py:139-172, with the
+ *   causal offset of attention_prefill.cu:103). Rows >= S_cache+S_q stay untouched.
+ * Requires S_cache + S_q <= S_max. */
+int pkb200_attention_prefill_kv_append(const void* Q, const void* K_new, const void* V_new,
+                                       void* K_cache, void* V_cache, void* O, int B, int H,
+                                       int S_q, int S_cache, int S_max, int D, float scale,
+                                       int causal, void* stream);
+
+/* Reads (and clears) the device-side error word that bounded waits inside the
+ * tensor-core kernels set on timeout (0 = none). Synchronises the device. */
+int pkb200_device_error(int* code);
+
+/* Counters of which implementation each entry point took since load:
+ * out[0] tcgen05 GEMM launches, out[1] SIMT GEMM launches,
+ * out[2] tcgen05 attention launches, out[3] SIMT attention launches,
+ * out[4] other kernels. Returns the number of counters written (<= n). */
+int pkb200_path_counters(long long* out, int n);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* ---- reference-compatible C++ entry points (same names, argument order and
+ * void return as kernels/generated/*.cu; errors are printed to stderr). */
+#include <cuda_bf16.h>
+void launch_rmsnorm(const __nv_bfloat16* input, const __nv_bfloat16* weight,
+                    __nv_bfloat16* output, int rows, int cols, float epsilon, void* stream);
+void launch_gelu(const __nv_bfloat16* input, __nv_bfloat16* output, int n, void* stream);
+void launch_matmul(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M,
+                   int N, int K, void* stream);
+void launch_fused_rmsnorm_matmul(const __nv_bfloat16* input, const __nv_bfloat16* weight,
+                                 __nv_bfloat16* output, int M, int N, int K, float epsilon,
+                                 void* stream);
+void launch_fused_matmul_bias_gelu(const __nv_bfloat16* a, const __nv_bfloat16* b,
+                                   const __nv_bfloat16* bias, __nv_bfloat16* output, int M,
+                                   int N, int K, void* stream);
+void launch_attention_prefill(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                              const __nv_bfloat16* V, __nv_bfloat16* O, int B, int H, int S_q,
+                              int S_kv, int D, float scale, int causal, void* stream);
+void launch_kv_cache_update(const __nv_bfloat16* cache, const __nv_bfloat16* new_rows,
+                            __nv_bfloat16* out, int B, int H, int S_cache, int S_new, int D,
+                            void* stream);
+void launch_matmul_int8(const __nv_bfloat16* A, const int8_t* Wq, const float* scale,
+                        __nv_bfloat16* C, int M, int N, int K, void* stream);
+#endif
+
+#endif /* PKB200_H */

@@ -1,0 +1,288 @@
+// gemm_tc.cuh - persistent tcgen05 GEMM with fused epilogues (sm_100a).
+//
+//   C[M,N] = epilogue( A[M,K] @ B[K,N] )   A, B, C bf16 row-major, fp32 accumulate.
+//
+// This is the contraction behind every matmul-shaped entry point of the
+// reference kernel library (kernels/generated/matmul.cu:78 launch_matmul,
+// fused_matmul_bias_gelu.cu:104, fused_rmsnorm_matmul.cu:114,
+// matmul_int8.cu:97) and of the MLP block composed in tests/e2e/conftest.py:104-107.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0   TMA producer: A tile 128x64 (K-major, 128B swizzle) and B tile
+//            64x256 as four 64x64 N-major boxes, into a STAGES-deep ring.
+//   warp 1   TMEM allocator + single-thread tcgen05.mma issuer
+//            (M=128, N=256, K=16 per instruction, 4 per stage).
+//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time from the finished
+//            accumulator, apply the fused epilogue with the reference's
+//            rounding points, 16-byte vector stores.
+//   The accumulator is double buffered in TMEM (2 x 256 fp32 columns), so the
+//   epilogue of tile t overlaps the mainloop of tile t+1.
+//
+// Rounding contract (tests/golden/golden.py:1-18): every op rounds its output
+// to bf16, so the epilogues round after the matmul, after each bias/residual
+// add and after GELU, exactly where the golden composition does.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace pkb200 {
+
+enum EpilogueKind : int {
+  kEpiPlain = 0,      // C = bf16(acc)                                  (matmul.cu)
+  kEpiBiasGelu = 1,   // C = bf16(gelu(bf16(bf16(acc) + bias)))         (fused_matmul_bias_gelu.cu)
+  kEpiBiasResid = 2,  // C = bf16(bf16(bf16(acc) + bias) + resid)       (MLP GEMM2 + residual)
+  kEpiColScale = 3,   // C = bf16(acc * scale[n])                       (matmul_int8.cu)
+  kEpiF32 = 4,        // C(fp32) = acc   (tensor-parallel partial sums)
+};
+
+struct EpilogueArgs {
+  const __nv_bfloat16* bias;   // [N] or null
+  const __nv_bfloat16* resid;  // [M, ld_resid] or null
+  const float* col_scale;      // [N] or null
+  long long ld_resid;
+};
+
+// GELU exactly as the golden writes it (tests/golden/golden.py:63-66):
+// 0.5 * x * (1 + erf(x * (1/sqrt(2)))) with the product x*(1/sqrt 2) in fp32.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float e = erff(x * 0.70710678118654752440f);
+  return (0.5f * x) * (1.0f + e);
+}
+
+// Apply epilogue `EPI` to 8 consecutive columns and return them packed as bf16.
+template <int EPI>
+__device__ __forceinline__ uint4 epilogue8(const float (&acc)[8], const EpilogueArgs& ea,
+                                           long long m, int n) {
+  float v[8];
+  if constexpr (EPI == kEpiPlain) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = acc[j];
+  } else if constexpr (EPI == kEpiBiasGelu) {
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(ea.bias + n));
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 bb = unpack_bf16x2(bw[j]);
+      const float u0 = bf16_round(bf16_round(acc[2 * j]) + bb.x);
+      const float u1 = bf16_round(bf16_round(acc[2 * j + 1]) + bb.y);
+      v[2 * j] = gelu_erf(u0);
+      v[2 * j + 1] = gelu_erf(u1);
+    }
+  } else if constexpr (EPI == kEpiBiasResid) {
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(ea.bias + n));
+    const uint4 r = *reinterpret_cast<const uint4*>(ea.resid + m * ea.ld_resid + n);
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+    const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 bb = unpack_bf16x2(bw[j]);
+      const float2 rr = unpack_bf16x2(rw[j]);
+      v[2 * j] = bf16_round(bf16_round(acc[2 * j]) + bb.x) + rr.x;
+      v[2 * j + 1] = bf16_round(bf16_round(acc[2 * j + 1]) + bb.y) + rr.y;
+    }
+  } else if constexpr (EPI == kEpiColScale) {
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(ea.col_scale + n));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(ea.col_scale + n + 4));
+    v[0] = acc[0] * s0.x; v[1] = acc[1] * s0.y; v[2] = acc[2] * s0.z; v[3] = acc[3] * s0.w;
+    v[4] = acc[4] * s1.x; v[5] = acc[5] * s1.y; v[6] = acc[6] * s1.z; v[7] = acc[7] * s1.w;
+  }
+  uint4 out;
+  out.x = pack_bf16x2(v[0], v[1]);
+  out.y = pack_bf16x2(v[2], v[3]);
+  out.z = pack_bf16x2(v[4], v[5]);
+  out.w = pack_bf16x2(v[6], v[7]);
+  return out;
+}
+
+namespace gemm {
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;       // 16 KB
+constexpr int B_BYTES = BK * BN * 2;       // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int B_BLOCK_BYTES = BK * 64 * 2;  // one 64-wide N block: 8 KB
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;             // 2 accumulators x 256 fp32 columns
+constexpr int GROUP_M = 16;                // rasterisation group (L2 reuse)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+}  // namespace gemm
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int per_group = gemm::GROUP_M * tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * gemm::GROUP_M;
+  const int gm = min(gemm::GROUP_M, tiles_m - first_m);
+  const int local = t - g * per_group;
+  mb = first_m + local % gm;
+  nb = local / gm;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b, void* __restrict__ C, long long ldc,
+                   int M, int N, int K, EpilogueArgs ea, int* err) {
+  using namespace gemm;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int tiles_m = (M + BM - 1) / BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer --
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+          tma_load_2d(sa, &map_a, &full_bar[stage], kb * BK, mb * BM);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(sb + j * B_BLOCK_BYTES, &map_b, &full_bar[stage], nb * BN + j * 64, kb * BK);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issuer --
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err, abort_flag, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, err, abort_flag, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = make_sw128_desc(b_addr + kk * 2048, B_BLOCK_BYTES, 1024);
+            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) tc_commit(&tfull_bar[acc]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue --
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, err, abort_flag, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const long long m = static_cast<long long>(mb) * BM + row;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int n0 = nb * BN + c * 32;
+        if (m < M) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int n = n0 + g * 8;
+            if (n < N) {
+              float a8[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(r[g * 8 + j]);
+              if constexpr (EPI == kEpiF32) {
+                float* cp = static_cast<float*>(C) + m * ldc + n;
+                reinterpret_cast<float4*>(cp)[0] = make_float4(a8[0], a8[1], a8[2], a8[3]);
+                reinterpret_cast<float4*>(cp)[1] = make_float4(a8[4], a8[5], a8[6], a8[7]);
+              } else {
+                const uint4 o = epilogue8<EPI>(a8, ea, m, n);
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(C) + m * ldc + n) = o;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace pkb200

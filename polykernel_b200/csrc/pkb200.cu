@@ -1,0 +1,668 @@
+// pkb200.cu - the C ABI (include/pkb200.h) and the reference-compatible
+// launch_* C++ symbols of libpkb200.so. Host-side dispatch: shape/alignment
+// validation, TMA descriptor encoding, and the choice between the tcgen05
+// paths and the bounds-checked SIMT paths.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "attention_tc.cuh"
+#include "simt_kernels.cuh"
+#include "../../include/pkb200.h"
+
+using namespace pkb200;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+__device__ int g_device_error;
+
+std::atomic<long long> g_counters[5];
+enum { kCntGemmTc = 0, kCntGemmSimt = 1, kCntAttnTc = 2, kCntAttnSimt = 3, kCntOther = 4 };
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool init = false;
+  int sms = 0;
+  int* err = nullptr;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int current_device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), g_device_error);
+    if (e != cudaSuccess) return e;
+    d.init = true;
+  }
+  *out = &d;
+  return cudaSuccess;
+}
+
+// ---------------------------------------------------------------- TMA maps --
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Rank-r tiled map with 128-byte swizzle. dims[0] is the contiguous axis.
+bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+              const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+              CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// --------------------------------------------------------------- workspace --
+// Grow-only device scratch owned by the library, one buffer per (device,
+// stream), for the entry points whose reference signature has no workspace
+// argument (launch_fused_rmsnorm_matmul, launch_matmul_int8).
+std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_ws;
+
+int library_workspace(size_t bytes, cudaStream_t s, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto& slot = g_ws[{dev, s}];
+  if (slot.second < bytes) {
+    if (slot.first) {
+      e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess) return e;
+      cudaFree(slot.first);
+      slot = {nullptr, 0};
+    }
+    e = cudaMalloc(&slot.first, bytes);
+    if (e != cudaSuccess) {
+      slot = {nullptr, 0};
+      return e;
+    }
+    slot.second = bytes;
+  }
+  *out = slot.first;
+  return cudaSuccess;
+}
+
+// -------------------------------------------------------------------- GEMM --
+template <int EPI>
+int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
+                   const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di) {
+  CUtensorMap ma, mb;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t str[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {64, gemm::BM};
+    if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, dims, str, box))
+      return cudaErrorInvalidValue;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K)};
+    const cuuint64_t str[1] = {static_cast<cuuint64_t>(N) * 2};
+    const cuuint32_t box[2] = {64, gemm::BK};
+    if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, dims, str, box))
+      return cudaErrorInvalidValue;
+  }
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
+  const int grid = tiles < di->sms ? tiles : di->sms;
+  gemm_tc_kernel<EPI><<<grid, gemm::NUM_THREADS, gemm::SMEM_BYTES, s>>>(
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
+  g_counters[kCntGemmTc]++;
+  return cudaGetLastError();
+}
+
+template <int EPI, typename TB>
+int launch_gemm_simt(const bf16* A, const TB* B, void* C, int M, int N, int K,
+                     const EpilogueArgs& ea, cudaStream_t s) {
+  dim3 grid((N + 31) / 32, (M + 31) / 32);
+  gemm_simt_kernel<EPI, TB><<<grid, 256, 0, s>>>(A, B, C, static_cast<long long>(N), M, N, K, ea);
+  g_counters[kCntGemmSimt]++;
+  return cudaGetLastError();
+}
+
+template <int EPI>
+int run_gemm(const bf16* A, const bf16* B, void* C, int M, int N, int K, const EpilogueArgs& ea,
+             cudaStream_t s) {
+  if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (!A || !B || !C) return cudaErrorInvalidValue;
+  if (EPI == kEpiBiasGelu || EPI == kEpiBiasResid) {
+    if (!ea.bias) return cudaErrorInvalidValue;
+  }
+  if (EPI == kEpiBiasResid && !ea.resid) return cudaErrorInvalidValue;
+  if (EPI == kEpiColScale && !ea.col_scale) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  const bool tc_ok = K > 0 && (K % 8) == 0 && (N % 8) == 0 && aligned16(A) && aligned16(B) &&
+                     aligned16(C) && (!ea.bias || aligned16(ea.bias)) &&
+                     (!ea.resid || aligned16(ea.resid)) &&
+                     (!ea.col_scale || aligned16(ea.col_scale)) && encode_fn() != nullptr;
+  if (tc_ok) return launch_gemm_tc<EPI>(A, B, C, M, N, K, ea, s, di);
+  return launch_gemm_simt<EPI, bf16>(A, B, C, M, N, K, ea, s);
+}
+
+// int8 -> bf16 weight expansion (exact: |q| <= 127 fits bf16's 8-bit significand).
+__global__ void int8_to_bf16_kernel(const int8_t* __restrict__ q, bf16* __restrict__ out,
+                                    long long n) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  for (; i + 8 <= n; i += stride * 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(q + i);
+    const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+    uint4 o;
+    o.x = pack_bf16x2(b[0], b[1]);
+    o.y = pack_bf16x2(b[2], b[3]);
+    o.z = pack_bf16x2(b[4], b[5]);
+    o.w = pack_bf16x2(b[6], b[7]);
+    *reinterpret_cast<uint4*>(out + i) = o;
+  }
+  for (; i < n; ++i) out[i] = __float2bfloat16_rn(static_cast<float>(q[i]));
+}
+
+__global__ void bias_residual_f32_kernel(const float* __restrict__ Y, const bf16* __restrict__ bias,
+                                         const bf16* __restrict__ resid, bf16* __restrict__ out,
+                                         long long M, int N) {
+  const long long total = M * N;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const int n = static_cast<int>(i % N);
+    const float u = bf16_round(bf16_round(Y[i]) + __bfloat162float(bias[n]));
+    out[i] = __float2bfloat16_rn(u + __bfloat162float(resid[i]));
+  }
+}
+
+int grid_for(long long work, int per_block, DeviceInfo* di) {
+  long long g = (work + per_block - 1) / per_block;
+  const long long cap = static_cast<long long>(di->sms) * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+int run_rmsnorm(const bf16* x, const bf16* w, bf16* y, long long rows, int cols, float eps,
+                cudaStream_t s) {
+  if (rows < 0 || cols < 0) return cudaErrorInvalidValue;
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  if (!x || !y) return cudaErrorInvalidValue;
+  const int rows_per_block = 8;
+  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  rmsnorm_rows_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, s>>>(x, w, y, rows,
+                                                                                   cols, eps);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
+int run_int8_expand(const int8_t* q, bf16* out, long long n, cudaStream_t s, DeviceInfo* di) {
+  int8_to_bf16_kernel<<<grid_for(n / 8 + 1, 256, di), 256, 0, s>>>(q, out, n);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
+
+// --------------------------------------------------------------- attention --
+template <int D>
+int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, int S_q,
+                          float scale, int causal, bf16* Kc, bf16* Vc, int S_max, int S_cache,
+                          cudaStream_t s, int* err) {
+  using L = attn::Layout<D>;
+  auto map3 = [](CUtensorMap* m, const void* base, int rows, long long rows_stride, int BH_) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(BH_)};
+    const cuuint64_t str[2] = {static_cast<cuuint64_t>(D) * 2,
+                               static_cast<cuuint64_t>(rows_stride) * D * 2};
+    const cuuint32_t box[3] = {64, 128, 1};
+    return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, str, box);
+  };
+  CUtensorMap mq, mka, mva, mkb, mvb, mks, mvs;
+  if (!map3(&mq, Q, S_q, S_q, BH)) return cudaErrorInvalidValue;
+  const bool has_a = kv.n_a > 0, has_b = kv.n_b > 0;
+  if (has_a) {
+    if (!map3(&mka, kv.Ka, kv.n_a, kv.lda_rows, BH) || !map3(&mva, kv.Va, kv.n_a, kv.lda_rows, BH))
+      return cudaErrorInvalidValue;
+  }
+  if (has_b) {
+    if (!map3(&mkb, kv.Kb, kv.n_b, kv.ldb_rows, BH) || !map3(&mvb, kv.Vb, kv.n_b, kv.ldb_rows, BH))
+      return cudaErrorInvalidValue;
+  }
+  if (!has_a) { mka = has_b ? mkb : mq; mva = has_b ? mvb : mq; }
+  if (!has_b) { mkb = mka; mvb = mva; }
+  const bool append = Kc != nullptr;
+  if (append) {
+    if (!map3(&mks, Kc, S_cache + S_q, S_max, BH) || !map3(&mvs, Vc, S_cache + S_q, S_max, BH))
+      return cudaErrorInvalidValue;
+  } else {
+    mks = mka;
+    mvs = mva;
+  }
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  AttnTcParams p{};
+  p.BH = BH;
+  p.S_q = S_q;
+  p.n_a = kv.n_a;
+  p.n_b = kv.n_b;
+  p.tiles_a = (kv.n_a + attn::BN - 1) / attn::BN;
+  p.tiles_b = (kv.n_b + attn::BN - 1) / attn::BN;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.append = append ? 1 : 0;
+  p.num_qtiles = (S_q + attn::BM - 1) / attn::BM;
+  p.O = O;
+  p.err = err;
+  dim3 grid(BH, p.num_qtiles);
+  attention_tc_kernel<D><<<grid, attn::NUM_THREADS, L::SMEM_BYTES, s>>>(mq, mka, mva, mkb, mvb,
+                                                                        mks, mvs, p);
+  return cudaGetLastError();
+}
+
+int launch_attention_tc(const bf16* Q, bf16* O, const KvSources& kv, int BH, int S_q, int D,
+                        float scale, int causal, bf16* Kc, bf16* Vc, int S_max, int S_cache,
+                        cudaStream_t s, int /*sms*/, int* err) {
+  if (encode_fn() == nullptr) return cudaErrorNotSupported;
+  if (D == 128)
+    return launch_attention_tc_d<128>(Q, O, kv, BH, S_q, scale, causal, Kc, Vc, S_max, S_cache, s, err);
+  return launch_attention_tc_d<64>(Q, O, kv, BH, S_q, scale, causal, Kc, Vc, S_max, S_cache, s, err);
+}
+
+int run_attention(const bf16* Q, bf16* O, const KvSources& kv, int B, int H, int S_q, int D,
+                  float scale, int causal, cudaStream_t s, bf16* Kc_write, bf16* Vc_write,
+                  int S_max, int S_cache) {
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  const int BH = B * H;
+  if (attention_tc_supported(kv, S_q, D, Q, O)) {
+    e = launch_attention_tc(Q, O, kv, BH, S_q, D, scale, causal, Kc_write, Vc_write, S_max,
+                            S_cache, s, di->sms, di->err);
+    if (e == cudaSuccess) g_counters[kCntAttnTc]++;
+    return e;
+  }
+  // General path: append first (if requested), then attend.
+  if (Kc_write) {
+    const long long units = static_cast<long long>(BH) * S_q * D / 8 + 1;
+    kv_rows_copy_kernel<<<grid_for(units, 256, di), 256, 0, s>>>(kv.Kb, Kc_write, BH, S_q, S_q,
+                                                                 S_max, S_cache, D);
+    kv_rows_copy_kernel<<<grid_for(units, 256, di), 256, 0, s>>>(kv.Vb, Vc_write, BH, S_q, S_q,
+                                                                 S_max, S_cache, D);
+    g_counters[kCntOther] += 2;
+  }
+  const int warps = 4;
+  dim3 grid((S_q + warps - 1) / warps, BH);
+  attention_simt_kernel<<<grid, 32 * warps, 0, s>>>(Q, O, kv, S_q, D, scale, causal);
+  g_counters[kCntAttnSimt]++;
+  return cudaGetLastError();
+}
+
+// Element-wise epilogues of the int8 MLP chain (bias+GELU on H, bias+residual on Y).
+__global__ void pkb200_bias_gelu_inplace(bf16* h, const bf16* bias, long long n, int N) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    const float u = bf16_round(__bfloat162float(h[i]) + __bfloat162float(bias[i % N]));
+    h[i] = __float2bfloat16_rn(gelu_erf(u));
+  }
+}
+__global__ void pkb200_bias_residual_inplace(bf16* y, const bf16* bias, const bf16* x,
+                                             long long n, int N) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    const float u = bf16_round(__bfloat162float(y[i]) + __bfloat162float(bias[i % N]));
+    y[i] = __float2bfloat16_rn(u + __bfloat162float(x[i]));
+  }
+}
+
+void report(const char* fn, int e) {
+  if (e != cudaSuccess)
+    std::fprintf(stderr, "[pkb200] %s failed: %s\n", fn,
+                 cudaGetErrorString(static_cast<cudaError_t>(e)));
+}
+
+inline cudaStream_t S(void* p) { return static_cast<cudaStream_t>(p); }
+inline const bf16* cb(const void* p) { return static_cast<const bf16*>(p); }
+inline bf16* b(void* p) { return static_cast<bf16*>(p); }
+
+size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+}  // namespace
+
+// =================================================================== C ABI ==
+extern "C" {
+
+const char* pkb200_version(void) { return "pkb200 0.1 sm_100a"; }
+
+int pkb200_rmsnorm(const void* input, const void* weight, void* output, int rows, int cols,
+                   float eps, void* stream) {
+  return run_rmsnorm(cb(input), cb(weight), b(output), rows, cols, eps, S(stream));
+}
+
+int pkb200_gelu(const void* input, void* output, long long n, void* stream) {
+  if (n < 0) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  if (!input || !output) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  gelu_kernel<<<grid_for(n, 256, di), 256, 0, S(stream)>>>(cb(input), b(output), n);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
+int pkb200_matmul(const void* A, const void* B, void* C, int M, int N, int K, void* stream) {
+  return run_gemm<kEpiPlain>(cb(A), cb(B), C, M, N, K, EpilogueArgs{}, S(stream));
+}
+
+int pkb200_matmul_f32out(const void* A, const void* B, float* C, int M, int N, int K,
+                         void* stream) {
+  return run_gemm<kEpiF32>(cb(A), cb(B), C, M, N, K, EpilogueArgs{}, S(stream));
+}
+
+int pkb200_fused_matmul_bias_gelu(const void* A, const void* B, const void* bias, void* out,
+                                  int M, int N, int K, void* stream) {
+  EpilogueArgs ea{};
+  ea.bias = cb(bias);
+  return run_gemm<kEpiBiasGelu>(cb(A), cb(B), out, M, N, K, ea, S(stream));
+}
+
+int pkb200_matmul_bias_residual(const void* A, const void* B, const void* bias,
+                                const void* resid, void* out, int M, int N, int K,
+                                void* stream) {
+  EpilogueArgs ea{};
+  ea.bias = cb(bias);
+  ea.resid = cb(resid);
+  ea.ld_resid = N;
+  return run_gemm<kEpiBiasResid>(cb(A), cb(B), out, M, N, K, ea, S(stream));
+}
+
+int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
+                             int M, int N, void* stream) {
+  if (M < 0 || N < 0) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (!Y || !bias || !resid || !out) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  bias_residual_f32_kernel<<<grid_for(static_cast<long long>(M) * N, 256, di), 256, 0,
+                             S(stream)>>>(Y, cb(bias), cb(resid), b(out), M, N);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
+int pkb200_fused_rmsnorm_matmul(const void* X, const void* W, const void* gamma, void* out,
+                                int M, int N, int K, float eps, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  void* ws = nullptr;
+  int e = library_workspace(align_up(static_cast<size_t>(M) * K * 2), S(stream), &ws);
+  if (e) return e;
+  e = run_rmsnorm(cb(X), cb(gamma), b(ws), M, K, eps, S(stream));
+  if (e) return e;
+  return run_gemm<kEpiPlain>(cb(ws), cb(W), out, M, N, K, EpilogueArgs{}, S(stream));
+}
+
+int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void* C, int M,
+                       int N, int K, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (!A || !Wq || !scale || !C) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  EpilogueArgs ea{};
+  ea.col_scale = scale;
+  const bool tc_shape = K > 0 && (K % 8) == 0 && (N % 8) == 0 && aligned16(A) && aligned16(C) &&
+                        aligned16(Wq) && aligned16(scale);
+  if (!tc_shape) return launch_gemm_simt<kEpiColScale, int8_t>(cb(A), Wq, C, M, N, K, ea, S(stream));
+  void* ws = nullptr;
+  e = library_workspace(align_up(static_cast<size_t>(K) * N * 2), S(stream), &ws);
+  if (e) return e;
+  e = run_int8_expand(Wq, b(ws), static_cast<long long>(K) * N, S(stream), di);
+  if (e) return e;
+  return run_gemm<kEpiColScale>(cb(A), cb(ws), C, M, N, K, ea, S(stream));
+}
+
+size_t pkb200_mlp_block_workspace_size(int M, int d, int ffn) {
+  if (M <= 0 || d <= 0 || ffn <= 0) return 0;
+  const size_t xn = align_up(static_cast<size_t>(M) * d * 2);
+  const size_t h = align_up(static_cast<size_t>(M) * ffn * 2);
+  const size_t wexp = align_up(static_cast<size_t>(d) * ffn * 2);  // int8 path only
+  return xn + h + wexp;
+}
+
+int pkb200_mlp_block(const void* X, const void* gamma, const void* W1, const void* b1,
+                     const void* W2, const void* b2, void* Y, int M, int d, int ffn, float eps,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || d <= 0 || ffn <= 0) return cudaErrorInvalidValue;
+  if (M == 0) return cudaSuccess;
+  if (!X || !W1 || !b1 || !W2 || !b2 || !Y || !workspace) return cudaErrorInvalidValue;
+  const size_t xn_bytes = align_up(static_cast<size_t>(M) * d * 2);
+  const size_t h_bytes = align_up(static_cast<size_t>(M) * ffn * 2);
+  if (workspace_bytes < xn_bytes + h_bytes) return cudaErrorInvalidValue;
+  bf16* xn = b(workspace);
+  bf16* h = reinterpret_cast<bf16*>(static_cast<char*>(workspace) + xn_bytes);
+  int e = run_rmsnorm(cb(X), cb(gamma), xn, M, d, eps, S(stream));
+  if (e) return e;
+  e = pkb200_fused_matmul_bias_gelu(xn, W1, b1, h, M, ffn, d, stream);
+  if (e) return e;
+  return pkb200_matmul_bias_residual(h, W2, b2, X, Y, M, d, ffn, stream);
+}
+
+int pkb200_mlp_block_int8(const void* X, const void* gamma, const int8_t* W1q,
+                          const float* s1, const void* b1, const int8_t* W2q, const float* s2,
+                          const void* b2, void* Y, int M, int d, int ffn, float eps,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || d <= 0 || ffn <= 0) return cudaErrorInvalidValue;
+  if (M == 0) return cudaSuccess;
+  if (!X || !W1q || !s1 || !b1 || !W2q || !s2 || !b2 || !Y || !workspace)
+    return cudaErrorInvalidValue;
+  if (workspace_bytes < pkb200_mlp_block_workspace_size(M, d, ffn)) return cudaErrorInvalidValue;
+  const size_t xn_bytes = align_up(static_cast<size_t>(M) * d * 2);
+  const size_t h_bytes = align_up(static_cast<size_t>(M) * ffn * 2);
+  bf16* xn = b(workspace);
+  bf16* h = reinterpret_cast<bf16*>(static_cast<char*>(workspace) + xn_bytes);
+  bf16* t = reinterpret_cast<bf16*>(static_cast<char*>(workspace) + xn_bytes + h_bytes);
+  bf16* wexp = t;  // reused for W1 then W2 (both d*ffn elements)
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  e = run_rmsnorm(cb(X), cb(gamma), xn, M, d, eps, S(stream));
+  if (e) return e;
+  // GEMM1: int8 matmul with per-channel scale, then bias + GELU as separate
+  // bf16 rounding steps (matmul_int8 -> bias -> gelu, each rounded).
+  e = run_int8_expand(W1q, wexp, static_cast<long long>(d) * ffn, S(stream), di);
+  if (e) return e;
+  EpilogueArgs ea{};
+  ea.col_scale = s1;
+  e = run_gemm<kEpiColScale>(xn, wexp, h, M, ffn, d, ea, S(stream));
+  if (e) return e;
+  // bias + GELU on H in place: reuse the SIMT elementwise path via a tiny kernel.
+  // (H = bf16(gelu(bf16(H + b1))))
+  {
+    const long long n = static_cast<long long>(M) * ffn;
+    pkb200_bias_gelu_inplace<<<grid_for(n, 256, di), 256, 0, S(stream)>>>(h, cb(b1), n, ffn);
+    g_counters[kCntOther]++;
+    e = cudaGetLastError();
+    if (e) return e;
+  }
+  e = run_int8_expand(W2q, wexp, static_cast<long long>(ffn) * d, S(stream), di);
+  if (e) return e;
+  ea.col_scale = s2;
+  e = run_gemm<kEpiColScale>(h, wexp, Y, M, d, ffn, ea, S(stream));
+  if (e) return e;
+  const long long n = static_cast<long long>(M) * d;
+  pkb200_bias_residual_inplace<<<grid_for(n, 256, di), 256, 0, S(stream)>>>(b(Y), cb(b2), cb(X),
+                                                                           n, d);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
+int pkb200_attention_prefill(const void* Q, const void* K, const void* V, void* O, int B, int H,
+                             int S_q, int S_kv, int D, float scale, int causal, void* stream) {
+  if (B < 0 || H < 0 || S_q < 0 || S_kv < 0 || D <= 0 || D > 256) return cudaErrorInvalidValue;
+  if (B == 0 || H == 0 || S_q == 0) return cudaSuccess;
+  if (!Q || !K || !V || !O) return cudaErrorInvalidValue;
+  KvSources kv{cb(K), cb(V), S_kv, S_kv, nullptr, nullptr, 0, 0};
+  return run_attention(cb(Q), b(O), kv, B, H, S_q, D, scale, causal, S(stream), nullptr, nullptr,
+                       0, 0);
+}
+
+int pkb200_kv_cache_update(const void* cache, const void* new_rows, void* out, int B, int H,
+                           int S_cache, int S_new, int D, void* stream) {
+  if (B < 0 || H < 0 || S_cache < 0 || S_new < 0 || D < 0) return cudaErrorInvalidValue;
+  if (B == 0 || H == 0 || D == 0 || S_cache + S_new == 0) return cudaSuccess;
+  if (!out || (S_cache && !cache) || (S_new && !new_rows)) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  const int BH = B * H;
+  const int total = S_cache + S_new;
+  const bool vec_ok = (D % 8) == 0 && aligned16(out) && (!cache || aligned16(cache)) &&
+                      (!new_rows || aligned16(new_rows));
+  if (!vec_ok && (D % 8) == 0) {
+    // misaligned base pointers: fall back to element copies by treating rows as D=1 columns
+    if (S_cache)
+      kv_rows_copy_kernel<<<grid_for(static_cast<long long>(BH) * S_cache * D, 256, di), 256, 0,
+                            S(stream)>>>(cb(cache), b(out), BH, S_cache * D, S_cache * D,
+                                         total * D, 0, 1);
+    if (S_new)
+      kv_rows_copy_kernel<<<grid_for(static_cast<long long>(BH) * S_new * D, 256, di), 256, 0,
+                            S(stream)>>>(cb(new_rows), b(out), BH, S_new * D, S_new * D,
+                                         total * D, S_cache * D, 1);
+  } else {
+    if (S_cache)
+      kv_rows_copy_kernel<<<grid_for(static_cast<long long>(BH) * S_cache * D / 8 + 1, 256, di),
+                            256, 0, S(stream)>>>(cb(cache), b(out), BH, S_cache, S_cache, total,
+                                                 0, D);
+    if (S_new)
+      kv_rows_copy_kernel<<<grid_for(static_cast<long long>(BH) * S_new * D / 8 + 1, 256, di), 256,
+                            0, S(stream)>>>(cb(new_rows), b(out), BH, S_new, S_new, total,
+                                            S_cache, D);
+  }
+  g_counters[kCntOther] += (S_cache ? 1 : 0) + (S_new ? 1 : 0);
+  return cudaGetLastError();
+}
+
+int pkb200_attention_prefill_kv_append(const void* Q, const void* K_new, const void* V_new,
+                                       void* K_cache, void* V_cache, void* O, int B, int H,
+                                       int S_q, int S_cache, int S_max, int D, float scale,
+                                       int causal, void* stream) {
+  if (B < 0 || H < 0 || S_q < 0 || S_cache < 0 || D <= 0 || D > 256 || S_max < S_cache + S_q)
+    return cudaErrorInvalidValue;
+  if (B == 0 || H == 0 || S_q == 0) return cudaSuccess;
+  if (!Q || !K_new || !V_new || !K_cache || !V_cache || !O) return cudaErrorInvalidValue;
+  KvSources kv{cb(K_cache), cb(V_cache), S_cache, S_max, cb(K_new), cb(V_new), S_q, S_q};
+  return run_attention(cb(Q), b(O), kv, B, H, S_q, D, scale, causal, S(stream), b(K_cache),
+                       b(V_cache), S_max, S_cache);
+}
+
+int pkb200_device_error(int* code) {
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  e = cudaDeviceSynchronize();
+  if (e) return e;
+  int v = 0;
+  e = cudaMemcpy(&v, di->err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e) return e;
+  const int zero = 0;
+  e = cudaMemcpy(di->err, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (code) *code = v;
+  return e;
+}
+
+int pkb200_path_counters(long long* out, int n) {
+  int k = 0;
+  for (; k < n && k < 5; ++k) out[k] = g_counters[k].load();
+  return k;
+}
+
+}  // extern "C"
+
+// ============================================ reference-compatible C++ ABI ==
+void launch_rmsnorm(const bf16* input, const bf16* weight, bf16* output, int rows, int cols,
+                    float epsilon, void* stream) {
+  report("launch_rmsnorm", pkb200_rmsnorm(input, weight, output, rows, cols, epsilon, stream));
+}
+void launch_gelu(const bf16* input, bf16* output, int n, void* stream) {
+  report("launch_gelu", pkb200_gelu(input, output, n, stream));
+}
+void launch_matmul(const bf16* A, const bf16* B, bf16* C, int M, int N, int K, void* stream) {
+  report("launch_matmul", pkb200_matmul(A, B, C, M, N, K, stream));
+}
+void launch_fused_rmsnorm_matmul(const bf16* input, const bf16* weight, bf16* output, int M,
+                                 int N, int K, float epsilon, void* stream) {
+  report("launch_fused_rmsnorm_matmul",
+         pkb200_fused_rmsnorm_matmul(input, weight, nullptr, output, M, N, K, epsilon, stream));
+}
+void launch_fused_matmul_bias_gelu(const bf16* a, const bf16* b_, const bf16* bias, bf16* output,
+                                   int M, int N, int K, void* stream) {
+  report("launch_fused_matmul_bias_gelu",
+         pkb200_fused_matmul_bias_gelu(a, b_, bias, output, M, N, K, stream));
+}
+void launch_attention_prefill(const bf16* Q, const bf16* K, const bf16* V, bf16* O, int B, int H,
+                              int S_q, int S_kv, int D, float scale, int causal, void* stream) {
+  report("launch_attention_prefill",
+         pkb200_attention_prefill(Q, K, V, O, B, H, S_q, S_kv, D, scale, causal, stream));
+}
+void launch_kv_cache_update(const bf16* cache, const bf16* new_rows, bf16* out, int B, int H,
+                            int S_cache, int S_new, int D, void* stream) {
+  report("launch_kv_cache_update",
+         pkb200_kv_cache_update(cache, new_rows, out, B, H, S_cache, S_new, D, stream));
+}
+void launch_matmul_int8(const bf16* A, const int8_t* Wq, const float* scale, bf16* C, int M, int N,
+                        int K, void* stream) {
+  report("launch_matmul_int8", pkb200_matmul_int8(A, Wq, scale, C, M, N, K, stream));
+}

@@ -1,0 +1,150 @@
+"""CPU: the NumPy oracle pinned against the reference golden's fixtures and the
+reference's own C++ CPU code (oracle/_ref, built from its sources)."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from oracle import golden_np as O
+from oracle import metrics as Mx
+from tests.helpers import check_gate
+
+F = O.from_bits
+REF_LIB = os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref",
+                       "liboracle_ref.so")
+
+
+def test_bf16_rounding_rne_and_nan():
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5, np.inf, -0.0, 3.0e38], np.float32)
+    # 1 + 2^-8 is a tie -> even (1.0); 1 + 3*2^-8 -> rounds up to 1 + 2^-6
+    assert O.bf16(x)[0] == 1.0 and O.bf16(x)[1] == 1.0 and O.bf16(x)[2] == 1.015625
+    assert np.isinf(O.bf16(x)[4]) and np.signbit(O.bf16(x)[5])
+    assert np.isnan(O.bf16(np.array([np.nan], np.float32)))[0]
+
+
+def test_known_answers(golden):
+    g = golden("known")
+    mm = O.matmul(F(g["mm_a"]), F(g["mm_b"]))
+    assert np.array_equal(mm, np.array([[19, 22], [43, 50]], np.float32))
+    assert np.array_equal(O.to_bits(mm), g["mm_out"])
+    assert np.array_equal(O.to_bits(O.gelu(F(g["gelu_in"]))), g["gelu_out"])
+    assert O.gelu(F(g["gelu_in"]))[0] == 0.0
+    assert abs(O.gelu(F(g["gelu_in"]))[1] - 0.8413) < 4e-3
+    assert np.array_equal(O.to_bits(O.rmsnorm(F(g["rms_in"]))), g["rms_out"])
+
+
+def test_elementwise_bit_exact(golden):
+    g = golden("elementwise")
+    assert np.array_equal(O.to_bits(O.rmsnorm(F(g["rms_w_x"]), F(g["rms_w_w"]))), g["rms_w_out"])
+    assert np.array_equal(O.to_bits(O.rmsnorm(F(g["rms_odd_x"]))), g["rms_odd_out"])
+    assert np.array_equal(O.to_bits(O.gelu(F(g["gelu_x"]))), g["gelu_out"])
+
+
+@pytest.mark.parametrize("name", ["sq", "odd", "rect", "bigk", "tiles"])
+def test_gemm_family_bit_exact(golden, name):
+    g = golden("gemm")
+    a, b, bias = F(g[f"{name}_a"]), F(g[f"{name}_b"]), F(g[f"{name}_bias"])
+    assert np.array_equal(O.to_bits(O.matmul(a, b)), g[f"{name}_mm"])
+    assert np.array_equal(O.to_bits(O.fused_rmsnorm_matmul(a, b)), g[f"{name}_frm"])
+    assert np.array_equal(O.to_bits(O.fused_matmul_bias_gelu(a, b, bias)), g[f"{name}_fbg"])
+
+
+def test_config1_bit_exact(golden):
+    g = golden("config1")
+    out = O.fused_rmsnorm_matmul(F(g["x"]), F(g["w"]), F(g["gamma"]), 1e-6)
+    assert np.array_equal(O.to_bits(out), g["out"])
+
+
+@pytest.mark.parametrize("name", ["mini", "mid"])
+def test_mlp_block_bit_exact(golden, name):
+    g = golden("mlp")
+    a = {k: F(g[f"{name}_{k}"]) for k in ("x", "gamma", "w1", "b1", "w2", "b2")}
+    y = O.mlp_block(a["x"], a["gamma"], a["w1"], a["b1"], a["w2"], a["b2"], 1e-6)
+    assert np.array_equal(O.to_bits(y), g[f"{name}_y"])
+
+
+@pytest.mark.parametrize("name", ["sq32", "mh", "d40", "s33", "d128", "d64odd"])
+def test_attention_matches_golden(golden, name):
+    g = golden("attention")
+    o = O.attention_prefill(F(g[f"{name}_q"]), F(g[f"{name}_k"]), F(g[f"{name}_v"]), True)
+    # The golden divides by sqrt(D) and masks with an additive -1e9; the oracle
+    # multiplies by 1/sqrt(D) and masks with -inf: equal up to fp32 rounding.
+    check_gate(o, F(g[f"{name}_o"]), min_exact=0.97)
+
+
+def test_attention_full_matches_golden(golden):
+    g = golden("attention")
+    o = O.attention_prefill(F(g["full_q"]), F(g["full_k"]), F(g["full_v"]), False)
+    check_gate(o, F(g["full_o"]), min_exact=0.97)
+
+
+@pytest.mark.parametrize("name", ["app32", "app128", "app64odd"])
+def test_attention_append_matches_golden(golden, name):
+    g = golden("attention")
+    t = {k: F(g[f"{name}_{k}"]) for k in ("q", "kn", "vn", "kc", "vc", "o", "nk", "nv")}
+    B, H, Sc, D = t["kc"].shape
+    Sn = t["kn"].shape[2]
+    kc = np.zeros((B, H, Sc + Sn + 7, D), np.float32)
+    vc = np.zeros_like(kc)
+    kc[:, :, :Sc], vc[:, :, :Sc] = t["kc"], t["vc"]
+    o, nk, nv = O.attention_prefill_kv_append(t["q"], t["kn"], t["vn"], kc, vc, Sc)
+    check_gate(o, t["o"], min_exact=0.97)
+    assert np.array_equal(nk[:, :, :Sc + Sn], t["nk"]) and np.array_equal(nv[:, :, :Sc + Sn], t["nv"])
+    assert not nk[:, :, Sc + Sn:].any()
+
+
+def test_leaky_mask_fails_gate(golden):
+    # Negative pin (tests/kernels/test_attention.py:447-463): dropping the causal
+    # mask must fail the gate.
+    g = golden("attention")
+    leaked = O.attention_prefill(F(g["sq32_q"]), F(g["sq32_k"]), F(g["sq32_v"]), False)
+    assert Mx.cosine(leaked, F(g["sq32_o"])) < 0.99
+
+
+def test_int8_matches_quant_golden(golden):
+    g = golden("int8")
+    out = O.matmul_int8(F(g["a"]), g["wq"], g["scale"])
+    assert np.array_equal(O.to_bits(out), g["out"])
+    out = O.matmul_int8(F(g["a"]), g["wq_pc"], g["scale_pc"])
+    assert np.array_equal(O.to_bits(out), g["out_pc"])
+    # wrong per-channel scale must fail the quant gate (test_quant.py:224-260)
+    bad = O.matmul_int8(F(g["a"]), g["wq"], g["scale"][::-1].copy())
+    assert not Mx.passes(Mx.report(bad, F(g["out"])), quant=True)
+
+
+# ------------------------------------------------ reference C++ CPU (oracle/_ref)
+@pytest.fixture(scope="module")
+def reflib():
+    if not os.path.exists(REF_LIB):
+        pytest.skip("oracle/_ref not built (make -C oracle)")
+    lib = ctypes.CDLL(REF_LIB)
+    return lib
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def test_reference_cpu_mlp_matches_oracle(golden, reflib):
+    g = golden("mlp")
+    name = "mini"
+    x = g[f"{name}_x"]
+    M, d = x.shape
+    ffn = g[f"{name}_w1"].shape[1]
+    y = np.zeros_like(x)
+    args = [np.ascontiguousarray(g[f"{name}_{k}"]) for k in ("x", "gamma", "w1", "b1", "w2", "b2")]
+    reflib.ref_mlp_rows(*[_p(a) for a in args], _p(y), ctypes.c_int64(M), ctypes.c_int64(d),
+                        ctypes.c_int64(ffn), ctypes.c_float(1e-6))
+    # The C++ reference sums in a sequential order, NumPy in blocks: near-exact.
+    check_gate(F(y), F(g[f"{name}_y"]), rel_ceiling=5e-2, min_exact=0.95)
+
+
+def test_reference_cpu_fused_rmsnorm_matmul_matches_oracle(golden, reflib):
+    g = golden("gemm")
+    a, b = np.ascontiguousarray(g["sq_a"]), np.ascontiguousarray(g["sq_b"])
+    out = np.zeros((a.shape[0], b.shape[1]), np.uint16)
+    reflib.ref_fused_rmsnorm_matmul(_p(a), _p(b), _p(out), ctypes.c_int64(a.shape[0]),
+                                    ctypes.c_int64(b.shape[1]), ctypes.c_int64(a.shape[1]),
+                                    ctypes.c_float(1e-5))
+    check_gate(F(out), F(g["sq_frm"]), min_exact=0.95)
