@@ -1,0 +1,433 @@
+"""Benchmark of the hot path: fused MLP block (M=16384, d=8192,
+ffn=28672, tensor-parallel over N GPUs) + causal prefill attention with KV append
+(config 3: B=4, H=32, S=2048, D=128, heads sharded over N GPUs), bf16.
+
+One step = one MLP block forward and one attention prefill on synthetic,
+seeded inputs resident in HBM. `value` is the whole-job TFLOP/s of the step
+(algorithmic FLOPs of both parts / device time, max over ranks).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl pkb200|reference]
+
+`--impl reference` times the reference's own CPU implementation of the MLP
+chain (kernels/cpu built from its sources into oracle/_ref/) on a bounded row
+sample of the same workload, with all host threads, and prints the same JSON
+line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MLP_CFG = dict(M=16384, d=8192, ffn=28672, eps=1e-6)
+ATTN_CFG = dict(B=4, H=32, S=2048, D=128, S_max=4096)
+METRIC = "fused-MLP & attention TFLOP/s, % of bf16 peak, at 1/2/4/8 B200 vs CPU ref"
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "liboracle_ref.so")
+
+
+def mlp_flops(M, d, ffn):
+    return 4.0 * M * d * ffn
+
+
+def attn_flops(B, H, S, D, S_cache=0):
+    # causal: query i sees S_cache + i + 1 keys; 2 matmuls x 2 flops per MAC
+    return 4.0 * B * H * D * sum(S_cache + i + 1 for i in range(S))
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p.get("bf16_tflops_sustained"), p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ------------------------------------------------------------- CPU baseline --
+def cpu_mlp_rows_tflops(x_bits, gamma, w1, b1, w2, b2, rows_per_thread, threads):
+    """Time the reference's CPU MLP chain (oracle/_ref, built from the
+    reference's kernels/cpu sources) on `threads` x `rows_per_thread` rows in
+    parallel. Returns (TFLOP/s, seconds, rows)."""
+    import numpy as np
+    lib = ctypes.CDLL(REF_LIB)
+    d = x_bits.shape[1]
+    ffn = w1.shape[1]
+    rows = threads * rows_per_thread
+    xs = np.ascontiguousarray(x_bits[:rows])
+    ys = np.zeros_like(xs)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+
+    def work(t):
+        lo = t * rows_per_thread
+        lib.ref_mlp_rows(P(xs[lo:lo + rows_per_thread]), P(gamma), P(w1), P(b1), P(w2), P(b2),
+                         P(ys[lo:lo + rows_per_thread]), ctypes.c_int64(rows_per_thread),
+                         ctypes.c_int64(d), ctypes.c_int64(ffn), ctypes.c_float(1e-6))
+
+    ths = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    t0 = time.perf_counter()
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    dt = time.perf_counter() - t0
+    return mlp_flops(rows, d, ffn) / dt / 1e12, dt, rows
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def synthetic_host_weights(M, d, ffn, seed=0):
+    """Seeded synthetic MLP inputs with config-5 distributions, as bf16 bits
+    (numpy), for the CPU legs."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+
+    def bf(a):
+        u = np.ascontiguousarray(a.astype(np.float32)).view(np.uint32)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    x = bf(rng.standard_normal((M, d), dtype=np.float32))
+    gamma = bf(1 + 0.1 * rng.standard_normal(d, dtype=np.float32))
+    w1 = bf(rng.standard_normal((d, ffn), dtype=np.float32) / np.float32(math.sqrt(d)))
+    b1 = bf(0.02 * rng.standard_normal(ffn, dtype=np.float32))
+    w2 = bf(rng.standard_normal((ffn, d), dtype=np.float32) / np.float32(math.sqrt(ffn)))
+    b2 = bf(0.02 * rng.standard_normal(d, dtype=np.float32))
+    return x, gamma, w1, b1, w2, b2
+
+
+def run_reference_arm(args):
+    """--impl reference: the reference's CPU MLP chain, bounded row sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg = MLP_CFG
+    if not os.path.exists(REF_LIB):
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/liboracle_ref.so not built (make -C oracle)"}))
+        return 0
+    threads = host_threads()
+    # rows in the sample: one row per thread per step (~3.5 s per row per core at config 5)
+    sample_rows = threads
+    x, gamma, w1, b1, w2, b2 = synthetic_host_weights(sample_rows, cfg["d"], cfg["ffn"])
+    times = []
+    for i in range(args.warmup + args.steps):
+        _, dt, rows = cpu_mlp_rows_tflops(x, gamma, w1, b1, w2, b2, 1, threads)
+        if i >= args.warmup:
+            times.append(dt)
+    tot = sum(times)
+    flops = mlp_flops(sample_rows, cfg["d"], cfg["ffn"]) * len(times)
+    value = flops / tot / 1e12
+    sample = (f"{sample_rows} of {cfg['M']} token rows of the config-5 MLP block per step "
+              f"(work is linear in rows); attention part not run on CPU")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * tot / len(times), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config-5 distributions)",
+        "config": {"workload": "config5_mlp_block_rows", "M_sample": sample_rows, "d": cfg["d"],
+                   "ffn": cfg["ffn"], "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm --
+class ClockSampler:
+    def __init__(self, gpu_index, path):
+        self.path = path
+        self.proc = None
+        self.gpu = gpu_index
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            lines = [l.strip() for l in open(self.path) if l.strip()]
+        except Exception:
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in lines:
+            p = [c.strip() for c in l.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import polykernel_b200 as pk
+    from polykernel_b200 import ops
+    from polykernel_b200.tp import TensorParallelMLP, shard_range
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    pk.lib()
+
+    M, d, ffn, eps = MLP_CFG["M"], MLP_CFG["d"], MLP_CFG["ffn"], MLP_CFG["eps"]
+    B, H, S, D, S_max = (ATTN_CFG[k] for k in ("B", "H", "S", "D", "S_max"))
+    if H % world:
+        raise SystemExit(f"heads={H} not divisible by {world}")
+    Hl = H // world
+    flo, fhi = shard_range(ffn, rank, world)
+    Fl = fhi - flo
+
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    g0 = torch.Generator(device=dev).manual_seed(1234)  # replicated tensors: same on all ranks
+    bf = torch.bfloat16
+    x = torch.randn(M, d, device=dev, generator=g0).to(bf)
+    gamma = (1 + 0.1 * torch.randn(d, device=dev, generator=g0)).to(bf)
+    b2 = (0.02 * torch.randn(d, device=dev, generator=g0)).to(bf)
+    w1 = (torch.randn(d, Fl, device=dev, generator=g) / math.sqrt(d)).to(bf)
+    b1 = (0.02 * torch.randn(Fl, device=dev, generator=g)).to(bf)
+    w2 = (torch.randn(Fl, d, device=dev, generator=g) / math.sqrt(ffn)).to(bf)
+    q = torch.randn(B, Hl, S, D, device=dev, generator=g).to(bf)
+    kn = torch.randn(B, Hl, S, D, device=dev, generator=g).to(bf)
+    vn = torch.randn(B, Hl, S, D, device=dev, generator=g).to(bf)
+    kc = torch.zeros(B, Hl, S_max, D, device=dev, dtype=bf)
+    vc = torch.zeros(B, Hl, S_max, D, device=dev, dtype=bf)
+    o = torch.empty_like(q)
+    y = torch.empty_like(x)
+
+    if world == 1:
+        ws = ops.mlp_workspace(M, d, ffn, dev)
+        mlp = lambda xx, out: ops.mlp_block(xx, gamma, w1, b1, w2, b2, eps, ws, out)  # noqa
+        launches_per_step = 3 + 1
+    else:
+        tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks)
+
+        def mlp(xx, out):
+            out.copy_(tpm(xx))
+            return out
+        launches_per_step = 2 + 2 * args.tp_chunks + 1
+
+    stream = torch.cuda.current_stream()
+    # events around the dominant kernel (GEMM1 with the bias+GELU epilogue) are
+    # recorded by timing the MLP's GEMM1 separately in the same loop
+    xn = torch.empty_like(x)
+    h = torch.empty(M, Fl, device=dev, dtype=bf)
+
+    def step(xx, out_y, out_o):
+        mlp(xx, out_y)
+        ops.attention_prefill_kv_append(q, kn, vn, kc, vc, 0, True, out=out_o)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(x, y, o)
+    barrier()
+    peaks = load_peaks()
+    clk = ClockSampler(local, os.path.join(tempfile.gettempdir(), f"pkb200_clocks_{rank}.csv"))
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with clk:
+        time.sleep(0.3)
+        barrier()
+        t_start.record(stream)
+        for _ in range(args.steps):
+            step(x, y, o)
+        t_end.record(stream)
+        barrier()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    clocks = clk.summary()
+
+    # Dominant kernel (GEMM1 + bias + GELU over this rank's shard): CUDA events
+    # on the launching stream around each launch, same shapes as in the step.
+    ops.rmsnorm(x, gamma, eps)
+    k_ms = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    xn = ops.rmsnorm(x, gamma, eps)
+    for _ in range(2):
+        ops.fused_matmul_bias_gelu(xn, w1, b1)
+    barrier()
+    for a, b in ev:
+        a.record(stream)
+        ops.fused_matmul_bias_gelu(xn, w1, b1)
+        b.record(stream)
+    barrier()
+    k_ms = [a.elapsed_time(b) for a, b in ev]
+    gemm1_ms = statistics.mean(k_ms)
+    # Attention alone (same shapes), for its own roofline figure.
+    ea = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    for a, b in ea:
+        a.record(stream)
+        ops.attention_prefill_kv_append(q, kn, vn, kc, vc, 0, True, out=o)
+        b.record(stream)
+    barrier()
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ea)
+
+    # End to end through the public API with HOST buffers: pinned host X/Q/K/V
+    # in, this rank's Y rows and O out, every step.
+    xh = x.cpu().pin_memory()
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, kn, vn))
+    r_lo, r_hi = (M * rank) // world, (M * (rank + 1)) // world
+    yh = torch.empty(r_hi - r_lo, d, dtype=bf).pin_memory()
+    oh = torch.empty_like(o, device="cpu").pin_memory()
+    xd, qd, kd, vd = (torch.empty_like(t) for t in (x, q, kn, vn))
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        mlp(xd, y)
+        ops.attention_prefill_kv_append(qd, kd, vd, kc, vc, 0, True, out=o)
+        yh.copy_(y[r_lo:r_hi], non_blocking=True)
+        oh.copy_(o, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    h2d = (xh.numel() + qh.numel() + kh.numel() + vh.numel()) * 2
+    d2h = (yh.numel() + oh.numel()) * 2
+
+    def gmax(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms, gemm1_ms, attn_ms, e2e_ms = gmax(ms), gmax(gemm1_ms), gmax(attn_ms), gmax(e2e_ms)
+    err = pk.device_error()
+
+    total_flops = mlp_flops(M, d, ffn) + attn_flops(B, H, S, D)
+    value = total_flops / (ms * 1e-3) / 1e12
+    burst, sustained, hbm, kind = peaks
+    peak = sustained or burst
+    g1_flops = 2.0 * M * d * Fl
+    g1_tflops = g1_flops / (gemm1_ms * 1e-3) / 1e12
+    a_flops = attn_flops(B, Hl, S, D)
+    a_tflops = a_flops / (attn_ms * 1e-3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and os.path.exists(REF_LIB):
+        import numpy as np
+        threads = host_threads()
+        to_np = lambda t: t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa
+        tf, dt, rows = cpu_mlp_rows_tflops(to_np(x[:threads]), to_np(gamma), to_np(w1), to_np(b1),
+                                           to_np(w2), to_np(b2), 1, threads)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+               "sample": f"{rows} of {M} token rows of the config-5 MLP block "
+                         f"({dt:.1f} s; work is linear in rows)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; BASELINE config-5 / config-3 shapes and distributions)",
+            "config": {"workload": "config5_mlp_block+config3_attention_prefill_kv_append",
+                       "mlp": {"M": M, "d": d, "ffn": ffn}, "attention":
+                       {"B": B, "H": H, "S": S, "D": D, "S_cache": 0, "cache_rows": S_max},
+                       "parallelism": f"tp{world} (MLP) / heads{world} (attention)",
+                       "l2": "inputs larger than L2 (no flush needed)"},
+            "parts": {"mlp_tflops": mlp_flops(M, d, ffn) / ((ms - attn_ms) * 1e-3) / 1e12,
+                      "attention_ms": attn_ms, "attention_tflops_whole_job": a_tflops * world,
+                      "attention_frac_of_peak": a_tflops / burst},
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel<bias+GELU> (MLP GEMM1)",
+                         "achieved": g1_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": g1_tflops / peak,
+                         "peak_kind": f"{kind} bf16 {'sustained' if sustained else 'burst'}",
+                         "traffic": args.traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "device_error": err,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="pkb200", choices=["pkb200", "reference"])
+    ap.add_argument("--tp-chunks", type=int, default=4)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="DRAM bytes per GEMM1 launch from an ncu capture (scaled)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

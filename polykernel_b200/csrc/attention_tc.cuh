@@ -255,16 +255,18 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&s_free[st]);
 
-      float mx = -INFINITY;
+      // Row max over the valid keys (raw scores; scale > 0 so the max commutes).
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
-        const float v = c < nvalid ? __uint_as_float(s[c]) * p.scale_log2 : -INFINITY;
+        const float v = c < nvalid ? __uint_as_float(s[c]) : -INFINITY;
         s[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        mx4[c & 3] = fmaxf(mx4[c & 3], v);
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       const bool grow = m_new > m_run + kRescaleThreshold || (m_run == -INFINITY && m_new > -INFINITY);
-      const float alpha = grow ? (m_run == -INFINITY ? 0.f : exp2f(m_run - m_new)) : 1.f;
+      const float alpha = grow ? (m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new)) : 1.f;
       if (grow) m_run = m_new;
       const bool any_grow = __any_sync(0xffffffffu, grow) && j > 0;
       if (any_grow) {
@@ -294,15 +296,16 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
         if (!ok) break;
       }
       uint8_t* pbuf = smem + L::OFF_P + st * L::P_BYTES;
-      float lsum = 0.f;
+      // p = 2^(s * scale*log2e - m): one FFMA + one SFU op per score.
+      const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c8 = 0; c8 < BN / 8; ++c8) {
         float e[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float v = __uint_as_float(s[c8 * 8 + k]);
-          e[k] = (m_run == -INFINITY) ? 0.f : exp2f(v - m_run);
-          lsum += e[k];
+          e[k] = fast_exp2(fmaf(__uint_as_float(s[c8 * 8 + k]), p.scale_log2, neg_m));
+          ls4[k & 3] += e[k];
         }
         uint4 pk;
         pk.x = pack_bf16x2(e[0], e[1]);
@@ -314,6 +317,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
         uint8_t* dst = pbuf + sub * (BM * 128) + r * 128 + ((chunk ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = pk;
       }
+      const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       l_run += lsum;
       fence_proxy_async_smem();
       tc_fence_before();

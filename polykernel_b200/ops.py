@@ -125,14 +125,17 @@ def matmul_bias_residual(a, w, b, resid):
     return c
 
 
-def bias_residual_f32(y32, b, resid):
+def bias_residual_f32(y32, b, resid, out=None):
     """bf16(bf16(bf16(y32) + b) + resid) for fp32 partial-sum totals."""
     _req(y32, "y32", dtype=torch.float32)
     _req(b, "bias")
     _req(resid, "resid")
     N = b.numel()
     M = y32.numel() // N
-    out = torch.empty(y32.shape, dtype=BF16, device=y32.device)
+    if out is None:
+        out = torch.empty(y32.shape, dtype=BF16, device=y32.device)
+    else:
+        _req(out, "out")
     check(lib().pkb200_bias_residual_f32(_ptr(y32), _ptr(b), _ptr(resid), _ptr(out), M, N,
                                          _stream()), "bias_residual_f32")
     return out
