@@ -36,25 +36,34 @@ def check_gate(out_f32, ref_f32, rel_ceiling=Mx.MAX_REL_ERR_THRESHOLD, min_exact
     return m
 
 
-def check_parity(out_f32, golden_f32, ref64_f32, rel_ceiling=Mx.MAX_REL_ERR_THRESHOLD,
-                 min_exact=0.99):
+def check_parity(out_f32, golden_f32, ref64_f32=None, rel_ceiling=Mx.MAX_REL_ERR_THRESHOLD,
+                 min_exact=0.99, max_outlier_frac=1e-3):
     """Parity for reduction kernels (GEMM family, MLP chain).
 
-    Gate: cosine >= 0.999 and PCC >= 0.99 against the golden, a bit-exact floor,
-    and max_rel_err either within `rel_ceiling` of the golden or -- where
-    near-zero outputs make max_rel_err a measure of fp32 summation order
-    (the reference's own C++ CPU code misses 1e-2 against its golden there) --
-    no larger against the fp64-accumulated oracle than twice the golden's own
-    max_rel_err against it.
+    Gate: cosine >= 0.999 and PCC >= 0.99 against the golden, a bit-exact
+    floor, and max_rel_err <= `rel_ceiling` for every output except small ones.
+    Where an output is small against the tensor's scale (cancellation in a
+    sum of products, or in the residual add y = t + x with t ~ -x), a
+    difference in fp32 summation order is a large relative error: the
+    reference's own C++ CPU code misses 1e-2 against its golden there (22 of
+    65,536 outputs at BASELINE config 1). Such outputs may exceed the ceiling,
+    but only as a fraction <= max_outlier_frac of all outputs and each within
+    one bf16 ulp of the golden's rms (|a - r| <= 2^-8 * rms(golden)).
     """
     m = Mx.report(out_f32, golden_f32, ref64_f32)
-    g64 = Mx.max_rel_err(golden_f32, ref64_f32)
-    m["golden_rel_err_vs_fp64"] = g64
+    a = np.asarray(out_f32, np.float64).reshape(-1)
+    r = np.asarray(golden_f32, np.float64).reshape(-1)
+    rms = float(np.sqrt(np.mean(r * r))) if r.size else 0.0
+    rel = np.abs(a - r) / (np.abs(r) + Mx.REL_ERR_EPS)
+    bad = rel > rel_ceiling
+    m["outliers"] = int(bad.sum())
+    m["outlier_max_abs_err_over_rms"] = float(np.max(np.abs(a - r)[bad]) / rms) if bad.any() else 0.0
     assert m["cosine"] >= Mx.COSINE_THRESHOLD, m
     assert m["pcc"] >= Mx.PCC_THRESHOLD, m
     assert m["bit_exact"] >= min_exact, m
-    assert (m["max_rel_err"] <= rel_ceiling
-            or m["max_rel_err_vs_fp64"] <= max(2.0 * g64, rel_ceiling)), m
+    if bad.any():
+        assert bad.sum() <= max(1, max_outlier_frac * r.size), m
+        assert m["outlier_max_abs_err_over_rms"] <= 2.0 ** -8, m
     return m
 
 

@@ -65,10 +65,7 @@ def test_config1_fused_rmsnorm_matmul(golden, pk):
     out = f32_from_t(pk.ops.fused_rmsnorm_matmul(x, w, gamma, eps=1e-6))
     assert _used(pk, c0, "gemm_tc")
     ref64 = O.fused_rmsnorm_matmul(F(g["x"]), F(g["w"]), F(g["gamma"]), 1e-6, acc=np.float64)
-    m = Mx.report(out, F(g["out"]), ref64)
-    print("config1", m)
-    assert m["cosine"] >= 0.999 and m["pcc"] >= 0.99 and m["bit_exact"] >= 0.95
-    assert m["max_rel_err_vs_fp64"] <= 5e-2
+    print("config1", check_parity(out, F(g["out"]), ref64))
 
 
 @pytest.mark.parametrize("name", ["mini", "mid"])

@@ -148,3 +148,20 @@ def test_reference_cpu_fused_rmsnorm_matmul_matches_oracle(golden, reflib):
                                     ctypes.c_int64(b.shape[1]), ctypes.c_int64(a.shape[1]),
                                     ctypes.c_float(1e-5))
     check_gate(F(out), F(g["sq_frm"]), min_exact=0.95)
+
+
+def test_parity_rule_accepts_reference_cpu_at_config1(golden, reflib):
+    """The GPU parity rule (tests/helpers.check_parity) is pinned to the
+    reference's own behaviour: its C++ CPU code, run on BASELINE config 1,
+    passes it (while missing the strict max_rel_err <= 1e-2 on near-zero outputs)."""
+    from tests.helpers import check_parity
+    g = golden("config1")
+    x, w, gm = (np.ascontiguousarray(g[k]) for k in ("x", "w", "gamma"))
+    xn = np.zeros_like(x)
+    out = np.zeros((x.shape[0], w.shape[1]), np.uint16)
+    reflib.ref_rmsnorm(_p(x), _p(gm), _p(xn), ctypes.c_int64(128), ctypes.c_int64(512),
+                       ctypes.c_float(1e-6))
+    reflib.ref_matmul(_p(xn), _p(w), _p(out), ctypes.c_int64(128), ctypes.c_int64(512),
+                      ctypes.c_int64(512))
+    m = check_parity(F(out), F(g["out"]))
+    assert m["max_rel_err"] > Mx.MAX_REL_ERR_THRESHOLD  # the strict gate alone would reject it
