@@ -7,37 +7,41 @@
 // causal (attention_prefill.cu:103), softmax in fp32, P.V accumulated in fp32,
 // one bf16 rounding of O. Rows that see no key produce 0 (attention_prefill.cu:154).
 //
-// One CTA per (128-query tile, batch*head). Roles:
-//   warps 0-3  softmax: thread r owns query row r (= TMEM lane r). Reads the
-//              S row with tcgen05.ld, online max/sum in the exp2 domain,
-//              writes P (bf16) into shared memory in the 128B-swizzled K-major
-//              layout the PV MMA reads, rescales O in TMEM only when the row
-//              max grew by more than 2^8 (the result is exact either way:
-//              every P and the final sum use the same stale max), and at the
-//              end normalises O and stores it.
-//   warp 4     TMA producer: Q once; K and V tiles (128 keys) through two
-//              2-deep rings. For the append entry point, the CTA whose query
-//              tile matches a tile of new rows also writes those K/V tiles
-//              from shared memory into the cache with TMA stores, so the
-//              append costs no extra HBM read.
-//   warp 5     TMEM owner + single-thread MMA issuer. S_j = Q K_j^T into one of
-//              two TMEM S buffers; O += P_{j-1} V_{j-1} is issued after S_j so
-//              the tensor cores work on S_j while the softmax warps handle S_{j-1}.
-// TMEM: S0 cols [0,128), S1 [128,256), O [256, 256+D).
+// One CTA per (pair of 128-query tiles A and B, batch*head). Roles (320 threads):
+//   warps 0-3  softmax for tile A, warps 4-7 softmax for tile B. Thread r of a
+//              group owns query row r (= TMEM lane r). It reads its S row with
+//              tcgen05.ld, keeps the running max/sum in the exp2 domain, and
+//              writes P (bf16 pairs) back into the same TMEM columns with
+//              tcgen05.st, where the P.V MMA reads it as its A operand. O is
+//              rescaled in TMEM only when the row max grew by more than 2^8
+//              (exact: every P and the final sum use the same stale max). At
+//              the end the group normalises O and stores it.
+//   warp 8     TMA producer: Q tiles once; K and V tiles (128 keys) through two
+//              2-deep rings shared by both query tiles. For the append entry
+//              point, the CTA whose query tiles match a tile of new rows also
+//              writes those K/V tiles from shared memory into the cache with
+//              TMA stores, so the append costs no extra HBM read.
+//   warp 9     TMEM owner + single-thread MMA issuer. Order per key tile j:
+//              PV_A(j); S_A(j+1); PV_B(j); S_B(j+1). S_X(j+1) overwrites the TMEM
+//              columns that held P_X(j), so the issuer waits for PV_X(j) to
+//              complete first (PV_B(j) is queued meanwhile, keeping the tensor
+//              pipe busy). The two groups interleave: while one waits for its
+//              MMAs the other runs its exponentials.
+// TMEM (512 columns): S/P_A [0,128), S/P_B [128,256), O_A [256,256+D), O_B [384,384+D).
 //
 // Key positions come from two sources (KvSources): A (rows [0, n_a), the
 // cache prefix or the whole K/V of the plain entry point) and B (the new
-// rows, positions n_a + r). Tiles never straddle the two: a source's last tile
-// may be partial, and the keys past its end are masked.
+// rows, positions n_a + r). Key tiles never straddle the two: a source's last
+// tile may be partial, and the keys past its end are masked.
 #pragma once
 
 #include "simt_kernels.cuh"
 
 namespace pkb200 {
 namespace attn {
-constexpr int BM = 128;       // query rows per CTA
+constexpr int BM = 128;       // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;       // keys per tile
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
@@ -45,12 +49,10 @@ struct Layout {
   static constexpr int DBOX = D / 64;                 // 64-column boxes per row
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_Q = 0;                      // Q_A, Q_B
+  static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;    // 2 stages
+  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;   // 2 stages
+  static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 };
 }  // namespace attn
@@ -66,9 +68,24 @@ struct AttnTcParams {
   int causal;
   int append;     // 1: write source-B tiles into the cache maps
   int num_qtiles;
+  int num_pairs;
   __nv_bfloat16* O;
   int* err;
 };
+
+// Number of key tiles query tile `qt` visits (0 if the tile is past S_q).
+__device__ __forceinline__ int attn_tiles_for(const AttnTcParams& p, int qt) {
+  if (qt * attn::BM >= p.S_q) return 0;
+  const int S_kv = p.n_a + p.n_b;
+  const int last_row = min(qt * attn::BM + attn::BM - 1, p.S_q - 1);
+  const int limit_last = p.causal ? (S_kv - p.S_q + last_row) : (S_kv - 1);
+  int n = 0;
+  for (int j = 0; j < p.tiles_a + p.tiles_b; ++j) {
+    const int p0 = j < p.tiles_a ? j * attn::BN : p.n_a + (j - p.tiles_a) * attn::BN;
+    if (p0 <= limit_last) n = j + 1;
+  }
+  return n;
+}
 
 template <int D>
 __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
@@ -90,28 +107,21 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   uint64_t* k_empty = bars + 3;   // [2]
   uint64_t* v_full = bars + 5;    // [2]
   uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_free = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;   // [2]
-  uint64_t* pv_done = bars + 15;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* s_full = bars + 9;    // [2]  per query tile (A, B)
+  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* pv_done = bars + 13;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int bh = blockIdx.x;
-  const int qt = p.num_qtiles - 1 - static_cast<int>(blockIdx.y);  // heavy tiles first
-  const int q0 = qt * BM;
-  const int S_kv = p.n_a + p.n_b;
-  // Last key position any row of this tile may see.
-  const int last_row = min(q0 + BM - 1, p.S_q - 1);
-  const int limit_last = p.causal ? (S_kv - p.S_q + last_row) : (S_kv - 1);
-  // Number of key tiles this CTA visits (tile start positions are increasing).
-  int ntiles = 0;
-  for (int j = 0; j < p.tiles_a + p.tiles_b; ++j) {
-    const int p0 = j < p.tiles_a ? j * BN : p.n_a + (j - p.tiles_a) * BN;
-    if (p0 <= limit_last) ntiles = j + 1;
-  }
+  const int bh = blockIdx.y;
+  const int pair = p.num_pairs - 1 - static_cast<int>(blockIdx.x);  // heavy pairs first
+  const int qt_a = 2 * pair, qt_b = 2 * pair + 1;
+  const int n_tile0 = attn_tiles_for(p, qt_a);
+  const int n_tile1 = attn_tiles_for(p, qt_b);
+  const int nmax = max(n_tile0, n_tile1);
+  const bool valid_b = qt_b * BM < p.S_q;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -121,14 +131,13 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
       mbar_init(&pv_done[i], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -137,20 +146,25 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
-    if (lane == 0 && ntiles > 0) {
+  if (warp == 8) {
+    if (lane == 0 && nmax > 0) {
       // -------------------------------------------------------- producer --
       tma_prefetch_desc(&map_q);
-      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
+      mbar_arrive_expect_tx(q_full, (valid_b ? 2 : 1) * L::Q_BYTES);
 #pragma unroll
-      for (int c = 0; c < L::DBOX; ++c)
-        tma_load_3d(smem + L::OFF_Q + c * (BM * 128), &map_q, q_full, c * 64, q0, bh);
-      for (int j = 0; j < ntiles; ++j) {
+      for (int c = 0; c < L::DBOX; ++c) {
+        tma_load_3d(smem + L::OFF_Q + c * (BM * 128), &map_q, q_full, c * 64, qt_a * BM, bh);
+        if (valid_b)
+          tma_load_3d(smem + L::OFF_Q + L::Q_BYTES + c * (BM * 128), &map_q, q_full, c * 64,
+                      qt_b * BM, bh);
+      }
+      for (int j = 0; j < nmax; ++j) {
         const bool from_a = j < p.tiles_a;
         const int row0 = from_a ? j * BN : (j - p.tiles_a) * BN;
         const CUtensorMap* mk = from_a ? &map_ka : &map_kb;
         const CUtensorMap* mv = from_a ? &map_va : &map_vb;
-        const bool do_append = p.append && !from_a && (row0 / BN) == qt;
+        const int new_tile = row0 / BN;
+        const bool do_append = p.append && !from_a && (new_tile == qt_a || new_tile == qt_b);
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         uint8_t* sk = smem + L::OFF_K + st * L::KV_BYTES;
@@ -181,177 +195,191 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
       }
       bulk_wait_group0();
     }
-  } else if (warp == 5) {
-    if (lane == 0 && ntiles > 0) {
+  } else if (warp == 9) {
+    if (lane == 0 && nmax > 0) {
       // ------------------------------------------------------ MMA issuer --
       constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(BM, D, false, true);
-      const uint32_t q_addr = smem_u32(smem + L::OFF_Q);
-      const uint32_t o_tmem = tmem + 256;
       bool ok = mbar_wait(q_full, 0, p.err, abort_flag, kErrTimeoutMma);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&v_full[st], ph, p.err, abort_flag, kErrTimeoutMma)) return false;
-        if (!mbar_wait(&p_full[st], ph, p.err, abort_flag, kErrTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + L::OFF_P + st * L::P_BYTES);
-        const uint32_t v_addr = smem_u32(smem + L::OFF_V + st * L::KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = make_sw128_desc(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, BN * 128, 1024);
-          tc_mma_f16(o_tmem, ad, bd, idesc_o, (i | kk) != 0);
-        }
-        tc_commit(&v_empty[st]);
-        tc_commit(&pv_done[st]);
-        return true;
-      };
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, p.err, abort_flag, kErrTimeoutMma)) { ok = false; break; }
-        if (!mbar_wait(&s_free[st], ph ^ 1, p.err, abort_flag, kErrTimeoutMma)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + L::OFF_K + st * L::KV_BYTES);
-        const uint32_t s_tmem = tmem + st * BN;
+      auto issue_s = [&](int x, int j) {
+        const uint32_t q_addr = smem_u32(smem + L::OFF_Q + x * L::Q_BYTES);
+        const uint32_t k_addr = smem_u32(smem + L::OFF_K + (j & 1) * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint64_t ad = make_sw128_desc(q_addr + off, 16, 1024);
-          const uint64_t bd = make_sw128_desc(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-          tc_mma_f16(s_tmem, ad, bd, idesc_s, kk != 0);
+          const uint64_t bd = make_sw128_desc(k_addr + off, 16, 1024);
+          tc_mma_f16(tmem + x * BN, ad, bd, idesc_s, kk != 0);
         }
-        tc_commit(&k_empty[st]);
-        tc_commit(&s_full[st]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        tc_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t v_addr = smem_u32(smem + L::OFF_V + (j & 1) * L::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, BN * 128, 1024);
+          tc_mma_f16_tmem_a(tmem + 256 + x * 128, tmem + x * BN + kk * 8, bd, idesc_o,
+                            (j | kk) != 0);
+        }
+        tc_commit(&pv_done[x]);
+      };
+      // prologue: S for key tile 0
+      if (ok) ok = mbar_wait(&k_full[0], 0, p.err, abort_flag, kErrTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        if (n_tile0 > 0) issue_s(0, 0);
+        if (n_tile1 > 0) issue_s(1, 0);
+        tc_commit(&k_empty[0]);
       }
-      if (ok) issue_pv(ntiles - 1);
+      for (int j = 0; j < nmax && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int jn = j + 1;
+        bool v_ready = false, k_next_ready = false;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int nt = x == 0 ? n_tile0 : n_tile1;
+          if (!ok || j >= nt) continue;
+          if (!v_ready) {
+            ok = mbar_wait(&v_full[st], ph, p.err, abort_flag, kErrTimeoutMma);
+            v_ready = true;
+          }
+          if (ok) ok = mbar_wait(&p_full[x], j & 1, p.err, abort_flag, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(x, j);
+          if (jn < nt) {
+            if (!k_next_ready) {
+              ok = mbar_wait(&k_full[jn & 1], (jn >> 1) & 1, p.err, abort_flag, kErrTimeoutMma);
+              k_next_ready = true;
+            }
+            // S_X(j+1) reuses the TMEM columns P_X(j) occupies: wait for PV_X(j).
+            if (ok) ok = mbar_wait(&pv_done[x], j & 1, p.err, abort_flag, kErrTimeoutMma);
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(x, jn);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[st]);
+        if (k_next_ready) tc_commit(&k_empty[jn & 1]);
+      }
     }
   } else {
     // ----------------------------------------------------------- softmax --
-    const int r = warp * 32 + lane;  // query row within the tile == TMEM lane
-    const int qi = q0 + r;
+    const int x = warp >> 2;        // query tile A (0) or B (1)
+    const int qw = warp & 3;        // TMEM lane quarter
+    const int r = qw * 32 + lane;   // query row within the tile == TMEM lane
+    const int qt = x == 0 ? qt_a : qt_b;
+    const int qi = qt * BM + r;
+    const int ntiles = x == 0 ? n_tile0 : n_tile1;
+    const int S_kv = p.n_a + p.n_b;
     const int limit = p.causal ? (S_kv - p.S_q + qi) : (S_kv - 1);
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(qw * 32) << 16);
+    const uint32_t s_col = x * BN;
+    const uint32_t o_col = 256 + x * 128;
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
       const bool from_a = j < p.tiles_a;
       const int p0 = from_a ? j * BN : p.n_a + (j - p.tiles_a) * BN;
       const int cnt = from_a ? min(BN, p.n_a - j * BN) : min(BN, p.n_b - (j - p.tiles_a) * BN);
       const int nvalid = max(0, min(cnt, limit - p0 + 1));
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], ph, p.err, abort_flag, kErrTimeoutSoftmax));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, p.err, abort_flag,
+                                             kErrTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
       uint32_t s[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(lane_base + st * BN + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+        tmem_ld32(lane_base + s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);
 
       // Row max over the valid keys (raw scores; scale > 0 so the max commutes).
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (__all_sync(0xffffffffu, nvalid == BN)) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const float v = c < nvalid ? __uint_as_float(s[c]) : -INFINITY;
-        s[c] = __float_as_uint(v);
-        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+        for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(s[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const float v = c < nvalid ? __uint_as_float(s[c]) : -INFINITY;
+          s[c] = __float_as_uint(v);
+          mx4[c & 3] = fmaxf(mx4[c & 3], v);
+        }
       }
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       const bool grow = m_new > m_run + kRescaleThreshold || (m_run == -INFINITY && m_new > -INFINITY);
       const float alpha = grow ? (m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new)) : 1.f;
       if (grow) m_run = m_new;
-      const bool any_grow = __any_sync(0xffffffffu, grow) && j > 0;
-      if (any_grow) {
-        // O holds P_0..P_{j-1} V; wait for the last of them, then rescale.
-        const int pj = j - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[pj & 1], (pj >> 1) & 1, p.err, abort_flag,
-                                               kErrTimeoutSoftmax));
-        if (!ok) break;
-        tc_fence_after();
+      if (__any_sync(0xffffffffu, grow) && j > 0) {
+        // O_X holds P_0..P_{j-1} V and is complete: S_X(j) was issued only
+        // after PV_X(j-1) finished, and S_X(j) has completed.
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
-          tmem_ld32(lane_base + 256 + c * 32, o);
+          tmem_ld32(lane_base + o_col + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-          tmem_st32(lane_base + 256 + c * 32, o);
+          tmem_st32(lane_base + o_col + c * 32, o);
         }
-        tmem_st_wait();
       }
       l_run *= alpha;
-      // P buffer `st` is free once PV_{j-2} finished.
-      if (j >= 2) {
-        const int pj = j - 2;
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[pj & 1], (pj >> 1) & 1, p.err, abort_flag,
-                                               kErrTimeoutSoftmax));
-        if (!ok) break;
-      }
-      uint8_t* pbuf = smem + L::OFF_P + st * L::P_BYTES;
-      // p = 2^(s * scale*log2e - m): one FFMA + one SFU op per score.
+      // p = 2^(s * scale*log2e - m): one FFMA + one SFU op per score; P is
+      // packed to bf16 pairs in place of the first 64 S columns.
       const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
       float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c8 = 0; c8 < BN / 8; ++c8) {
-        float e[8];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          e[k] = fast_exp2(fmaf(__uint_as_float(s[c8 * 8 + k]), p.scale_log2, neg_m));
-          ls4[k & 3] += e[k];
+        for (int k = 0; k < 32; ++k) {
+          const float e0 = fast_exp2(fmaf(__uint_as_float(s[h * 64 + 2 * k]), p.scale_log2, neg_m));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(s[h * 64 + 2 * k + 1]), p.scale_log2, neg_m));
+          ls4[(2 * k) & 3] += e0;
+          ls4[(2 * k + 1) & 3] += e1;
+          pk[k] = pack_bf16x2(e0, e1);
         }
-        uint4 pk;
-        pk.x = pack_bf16x2(e[0], e[1]);
-        pk.y = pack_bf16x2(e[2], e[3]);
-        pk.z = pack_bf16x2(e[4], e[5]);
-        pk.w = pack_bf16x2(e[6], e[7]);
-        const int sub = c8 >> 3;          // which 64-key half
-        const int chunk = c8 & 7;         // 16-byte chunk within the 128-byte row
-        uint8_t* dst = pbuf + sub * (BM * 128) + r * 128 + ((chunk ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = pk;
+        tmem_st32(lane_base + s_col + h * 32, pk);
       }
-      const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
-      l_run += lsum;
-      fence_proxy_async_smem();
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[x]);
     }
     // ------------------------------------------------------- epilogue --
-    __nv_bfloat16* orow = p.O + (static_cast<long long>(bh) * p.S_q + qi) * D;
-    if (ntiles > 0 && ok) {
-      const int pj = ntiles - 1;
-      ok = mbar_wait(&pv_done[pj & 1], (pj >> 1) & 1, p.err, abort_flag, kErrTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    if (x == 0 || valid_b) {
+      __nv_bfloat16* orow = p.O + (static_cast<long long>(bh) * p.S_q + qi) * D;
+      if (ntiles > 0 && ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (ntiles - 1) & 1, p.err, abort_flag,
+                                               kErrTimeoutSoftmax));
+      }
+      if (ok) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        if (ntiles > 0) {
-          tmem_ld32(lane_base + 256 + c * 32, o);
-          tmem_ld_wait();
-        } else {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          if (ntiles > 0) {
+            tmem_ld32(lane_base + o_col + c * 32, o);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) o[k] = 0u;
-        }
-        if (qi < p.S_q) {
+            for (int k = 0; k < 32; ++k) o[k] = 0u;
+          }
+          if (qi < p.S_q) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
-            v.y = pack_bf16x2(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
-            v.z = pack_bf16x2(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
-            v.w = pack_bf16x2(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
+            for (int g = 0; g < 4; ++g) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
+              v.y = pack_bf16x2(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
+              v.z = pack_bf16x2(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
+              v.w = pack_bf16x2(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
+            }
           }
         }
       }
@@ -360,7 +388,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -372,6 +400,7 @@ inline bool attention_tc_supported(const KvSources& kv, int S_q, int D, const vo
   auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   if (!(D == 64 || D == 128)) return false;
   if (S_q <= 0) return false;
+  if (kv.n_a < 0 || kv.n_b < 0) return false;
   if (!al(Q) || !al(O)) return false;
   if (kv.n_a > 0 && (!al(kv.Ka) || !al(kv.Va))) return false;
   if (kv.n_b > 0 && (!al(kv.Kb) || !al(kv.Vb))) return false;

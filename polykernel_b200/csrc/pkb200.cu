@@ -300,9 +300,10 @@ int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, i
   p.causal = causal ? 1 : 0;
   p.append = append ? 1 : 0;
   p.num_qtiles = (S_q + attn::BM - 1) / attn::BM;
+  p.num_pairs = (p.num_qtiles + 1) / 2;
   p.O = O;
   p.err = err;
-  dim3 grid(BH, p.num_qtiles);
+  dim3 grid(p.num_pairs, BH);
   attention_tc_kernel<D><<<grid, attn::NUM_THREADS, L::SMEM_BYTES, s>>>(mq, mka, mva, mkb, mvb,
                                                                         mks, mvs, p);
   return cudaGetLastError();
@@ -324,7 +325,7 @@ int run_attention(const bf16* Q, bf16* O, const KvSources& kv, int B, int H, int
   int e = current_device_info(&di);
   if (e) return e;
   const int BH = B * H;
-  if (attention_tc_supported(kv, S_q, D, Q, O)) {
+  if (BH <= 65535 && attention_tc_supported(kv, S_q, D, Q, O)) {
     e = launch_attention_tc(Q, O, kv, BH, S_q, D, scale, causal, Kc_write, Vc_write, S_max,
                             S_cache, s, di->sms, di->err);
     if (e == cudaSuccess) g_counters[kCntAttnTc]++;

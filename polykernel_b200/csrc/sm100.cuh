@@ -179,6 +179,19 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]; kind::f16, A (K-major, bf16 pairs packed in
+// 32-bit columns, row m = TMEM lane m) read from tensor memory.
+__device__ __forceinline__ void tc_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem,
+                                                  uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when all previously issued tcgen05.mma of this thread
 // have completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
