@@ -55,6 +55,23 @@ int pkb200_matmul_f32out(const void* A, const void* B, float* C, int M, int N, i
 int pkb200_fused_rmsnorm_matmul(const void* X, const void* W, const void* gamma, void* out,
                                 int M, int N, int K, float eps, void* stream);
 
+/* Same result as pkb200_fused_rmsnorm_matmul, but this entry point allocates
+ * no device memory at all. It is for callers that cannot call cudaMalloc on
+ * the calling thread: code running while a CUDA graph is being captured,
+ * real-time or embedded hosts that forbid allocation after start-up, and
+ * plugins whose host application owns all memory. The normalised rows go to
+ * a fixed 16 MiB scratch array compiled into the library (each GPU that loads
+ * the library holds it until the process exits), so M*K must not exceed
+ * 8,388,608 elements; larger shapes return cudaErrorInvalidValue with a
+ * message on stderr. The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture. All calls share the one array: calls
+ * whose work overlaps on the GPU (different streams, or different host
+ * threads) race on it and must be serialised by the caller.
+ * This entry point has no counterpart in the reference. */
+int pkb200_fused_rmsnorm_matmul_noalloc(const void* X, const void* W, const void* gamma,
+                                        void* out, int M, int N, int K, float eps, void* stream);
+
 /* out = bf16(gelu(bf16(bf16(A @ B) + bias))). Replaces launch_fused_matmul_bias_gelu
  * (fused_matmul_bias_gelu.cu:104-106). */
 int pkb200_fused_matmul_bias_gelu(const void* A, const void* B, const void* bias, void* out,

@@ -22,6 +22,8 @@ SIGNATURES = {
     "pkb200_matmul": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_matmul_f32out": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_fused_rmsnorm_matmul": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P]),
+    "pkb200_fused_rmsnorm_matmul_noalloc": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int,
+                                                    c_float, _P]),
     "pkb200_fused_matmul_bias_gelu": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_matmul_bias_residual": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_bias_residual_f32": (c_int, [_P, _P, _P, _P, c_int, c_int, _P]),

@@ -378,6 +378,34 @@ inline bf16* b(void* p) { return static_cast<bf16*>(p); }
 
 size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// ------------------------------------------------- fixed device scratch --
+// Scratch for pkb200_fused_rmsnorm_matmul_noalloc: the normalised rows, at most
+// kNoAllocScratchElems bf16 values (16 MiB). It lives in the library's device
+// image, so every GPU that loads the library holds it until the process exits.
+constexpr long long kNoAllocScratchElems = 8LL * 1024 * 1024;
+static __device__ __align__(256) bf16 g_noalloc_scratch[kNoAllocScratchElems];
+
+// The device address of g_noalloc_scratch for each device. In host code the
+// array's name is only a host-side stand-in, so the address must come from
+// cudaGetSymbolAddress, called with that device current (first call per device).
+bf16* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(bf16** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = static_cast<bf16*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
 }  // namespace
 
 // =================================================================== C ABI ==
@@ -607,6 +635,27 @@ int pkb200_attention_prefill_kv_append(const void* Q, const void* K_new, const v
   KvSources kv{cb(K_cache), cb(V_cache), S_cache, S_max, cb(K_new), cb(V_new), S_q, S_q};
   return run_attention(cb(Q), b(O), kv, B, H, S_q, D, scale, causal, S(stream), b(K_cache),
                        b(V_cache), S_max, S_cache);
+}
+
+int pkb200_fused_rmsnorm_matmul_noalloc(const void* X, const void* W, const void* gamma,
+                                        void* out, int M, int N, int K, float eps, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (static_cast<long long>(M) * K > kNoAllocScratchElems) {
+    std::fprintf(stderr,
+                 "[pkb200] pkb200_fused_rmsnorm_matmul_noalloc: M*K = %lld exceeds the fixed "
+                 "scratch of %lld elements; use pkb200_fused_rmsnorm_matmul\n",
+                 static_cast<long long>(M) * K, kNoAllocScratchElems);
+    return cudaErrorInvalidValue;
+  }
+  bf16* ws = nullptr;
+  int e = noalloc_scratch(&ws);
+  if (e) return e;
+  // Every element of the M*K scratch rows is written by the RMSNorm pass before
+  // the GEMM reads it, so nothing left by an earlier call is used.
+  e = run_rmsnorm(cb(X), cb(gamma), ws, M, K, eps, S(stream));
+  if (e) return e;
+  return run_gemm<kEpiPlain>(ws, cb(W), out, M, N, K, EpilogueArgs{}, S(stream));
 }
 
 int pkb200_device_error(int* code) {
