@@ -290,62 +290,96 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
                                              kErrTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(lane_base + s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-      tmem_ld_wait();
-
-      // Row max over the valid keys (raw scores; scale > 0 so the max commutes).
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (__all_sync(0xffffffffu, nvalid == BN)) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(s[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const float v = c < nvalid ? __uint_as_float(s[c]) : -INFINITY;
-          s[c] = __float_as_uint(v);
-          mx4[c & 3] = fmaxf(mx4[c & 3], v);
-        }
-      }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
-      const float m_new = fmaxf(m_run, mx);
-      const bool grow = m_new > m_run + kRescaleThreshold || (m_run == -INFINITY && m_new > -INFINITY);
-      const float alpha = grow ? (m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new)) : 1.f;
-      if (grow) m_run = m_new;
-      if (__any_sync(0xffffffffu, grow) && j > 0) {
-        // O_X holds P_0..P_{j-1} V and is complete: S_X(j) was issued only
-        // after PV_X(j-1) finished, and S_X(j) has completed.
+      const bool full = __all_sync(0xffffffffu, nvalid == BN);
+      // The tile is processed in two halves of 64 keys. Half h reads S
+      // columns [64h, 64h+64) and writes its P (32 columns of bf16 pairs) to
+      // columns [32h, 32h+32), which the first half has already consumed.
+      // When the running max is known and the tile is fully visible, the
+      // exponentials use it straight away while the half's max is computed
+      // alongside; only if that max exceeds the running one by more than the
+      // rescale threshold is the half redone (rare). Otherwise the max comes
+      // first. When the max grows, O, the row sum, and (in the second half)
+      // the first half's P are rescaled, so P and the sum always share one max.
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(lane_base + o_col + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-          tmem_st32(lane_base + o_col + c * 32, o);
-        }
-      }
-      l_run *= alpha;
-      // p = 2^(s * scale*log2e - m): one FFMA + one SFU op per score; P is
-      // packed to bf16 pairs in place of the first 64 S columns.
-      const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
-      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
+        uint32_t sv[64];
+        tmem_ld32(lane_base + s_col + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(lane_base + s_col + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        if (!full) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(s[h * 64 + 2 * k]), p.scale_log2, neg_m));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(s[h * 64 + 2 * k + 1]), p.scale_log2, neg_m));
-          ls4[(2 * k) & 3] += e0;
-          ls4[(2 * k + 1) & 3] += e1;
-          pk[k] = pack_bf16x2(e0, e1);
+          for (int c = 0; c < 64; ++c)
+            if (h * 64 + c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
+        }
+        uint32_t pk[32];
+        float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        const bool optimistic = full && m_run != -INFINITY;
+        if (optimistic) {
+          const float neg_m = -m_run;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const float s0 = __uint_as_float(sv[2 * k]), s1 = __uint_as_float(sv[2 * k + 1]);
+            mx4[k & 3] = fmax3(mx4[k & 3], s0, s1);
+            const float e0 = fast_exp2(fmaf(s0, p.scale_log2, neg_m));
+            const float e1 = fast_exp2(fmaf(s1, p.scale_log2, neg_m));
+            ls4[(2 * k) & 3] += e0;
+            ls4[(2 * k + 1) & 3] += e1;
+            pk[k] = pack_bf16x2(e0, e1);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            mx4[k & 3] = fmax3(mx4[k & 3], __uint_as_float(sv[2 * k]), __uint_as_float(sv[2 * k + 1]));
+        }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+        const float m_new = fmaxf(m_run, mx);
+        const bool grow = m_new > m_run + kRescaleThreshold || (m_run == -INFINITY && m_new > -INFINITY);
+        const bool any_grow = __any_sync(0xffffffffu, grow);
+        if (!optimistic || any_grow) {
+          const float alpha = grow ? (m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new)) : 1.f;
+          if (grow) m_run = m_new;
+          if (any_grow && j > 0) {
+            // O_X holds P_0..P_{j-1} V and is complete: S_X(j) was issued only
+            // after PV_X(j-1) finished, and S_X(j) has completed.
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(lane_base + o_col + c * 32, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+              tmem_st32(lane_base + o_col + c * 32, o);
+            }
+          }
+          if (any_grow && h == 1) {
+            // the first half's P was made with the old max
+            uint32_t q[32];
+            tmem_ld32(lane_base + s_col, q);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const float2 f = unpack_bf16x2(q[k]);
+              q[k] = pack_bf16x2(f.x * alpha, f.y * alpha);
+            }
+            tmem_st32(lane_base + s_col, q);
+          }
+          l_run *= alpha;
+          const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) ls4[q] = 0.f;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const float e0 = fast_exp2(fmaf(__uint_as_float(sv[2 * k]), p.scale_log2, neg_m));
+            const float e1 = fast_exp2(fmaf(__uint_as_float(sv[2 * k + 1]), p.scale_log2, neg_m));
+            ls4[(2 * k) & 3] += e0;
+            ls4[(2 * k + 1) & 3] += e1;
+            pk[k] = pack_bf16x2(e0, e1);
+          }
         }
         tmem_st32(lane_base + s_col + h * 32, pk);
+        l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       }
-      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
