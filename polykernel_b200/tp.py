@@ -8,9 +8,10 @@ exchange; the bias + residual epilogue runs after it. Summing fp32 partials and
 rounding once to bf16 keeps the golden's rounding points (golden.py:48-60):
 only the fp32 summation order changes.
 
-The reference has no multi-GPU path; this is new. The rows of GEMM2 are
-processed in `chunks` so that the all-reduce of chunk i (on a side stream)
-overlaps GEMM2 of chunk i+1.
+The reference has no multi-GPU path; this is new. With `chunks` > 1
+the rows of GEMM2 are processed in chunks whose reduction (reduce-scatter of
+the fp32 partials, epilogue on this rank's rows, all-gather of the bf16
+result) runs on a side stream and overlaps GEMM2 of the next chunk.
 """
 from __future__ import annotations
 
@@ -69,22 +70,41 @@ class TensorParallelMLP:
             y32 = k.matmul_f32out(h, self.w2)
             dist.all_reduce(y32, group=self.group)
             return k.bias_residual_f32(y32, self.b2, x)
-        # Chunked: GEMM2 of chunk i+1 overlaps the all-reduce of chunk i.
+        return self._pipelined(x, h, M)
+
+    def _pipelined(self, x, h, M):
+        """GEMM2 in row chunks; each chunk's fp32 partials are reduce-scattered
+        (rank r receives the sum of the chunk's r-th row block), the bias +
+        residual epilogue runs on those rows, and an all-gather of the bf16
+        result rebuilds the chunk on every rank. The collectives and the
+        epilogue of chunk i run on a side stream while GEMM2 of chunk i+1 runs.
+        Reduce-scatter + all-gather of bf16 moves 25% fewer bytes than an
+        all-reduce of the fp32 partials."""
+        k = self.kern
+        W = self.world
+        rank = dist.get_rank(self.group)
         comm = self._comm_stream(x)
         main = torch.cuda.current_stream()
         out = torch.empty_like(x)
-        bounds = [(M * i) // self.chunks for i in range(self.chunks + 1)]
-        pending = []
+        rows = M // self.chunks
+        if rows * self.chunks != M or rows % W:
+            raise ValueError(f"M={M} must split into {self.chunks} chunks of a multiple of {W} rows")
+        per = rows // W
+        keep = []
         for i in range(self.chunks):
-            lo, hi = bounds[i], bounds[i + 1]
-            y32 = k.matmul_f32out(h[lo:hi], self.w2)
+            lo = i * rows
+            y32 = k.matmul_f32out(h[lo:lo + rows], self.w2)
             ev = torch.cuda.Event()
             ev.record(main)
             with torch.cuda.stream(comm):
                 comm.wait_event(ev)
-                dist.all_reduce(y32, group=self.group)
-                k.bias_residual_f32(y32, self.b2, x[lo:hi], out=out[lo:hi])
-                y32.record_stream(comm)
-            pending.append(y32)
+                part = torch.empty(per, y32.shape[1], dtype=torch.float32, device=x.device)
+                dist.reduce_scatter_tensor(part, y32, group=self.group)
+                r0 = lo + rank * per
+                mine = k.bias_residual_f32(part, self.b2, x[r0:r0 + per])
+                dist.all_gather_into_tensor(out[lo:lo + rows], mine, group=self.group)
+                for t in (y32, part, mine):
+                    t.record_stream(comm)
+            keep.append(y32)
         main.wait_stream(comm)
         return out
