@@ -419,7 +419,9 @@ def main():
     ap.add_argument("--impl", default="pkb200", choices=["pkb200", "reference"])
     ap.add_argument("--tp-chunks", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--traffic", type=float, default=None,
+    # DRAM bytes per config-5 GEMM1 launch: 1.71 GB measured by ncu at M=4096
+    # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).
+    ap.add_argument("--traffic", type=float, default=6.83e9,
                     help="DRAM bytes per GEMM1 launch from an ncu capture (scaled)")
     args = ap.parse_args()
     if args.warmup < 3:
