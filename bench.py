@@ -250,12 +250,13 @@ def run_gpu_arm(args):
         mlp = lambda xx, out: ops.mlp_block(xx, gamma, w1, b1, w2, b2, eps, ws, out)  # noqa
         launches_per_step = 3 + 1
     else:
-        tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks)
+        tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks,
+                                fused_reduce=args.tp_mode == "fused")
 
         def mlp(xx, out):
             out.copy_(tpm(xx))
             return out
-        launches_per_step = 2 + 2 * args.tp_chunks + 1
+        launches_per_step = (2 + 2 + 1) if args.tp_mode == "fused" else (2 + 2 * args.tp_chunks + 1)
 
     stream = torch.cuda.current_stream()
     # events around the dominant kernel (GEMM1 with the bias+GELU epilogue) are
@@ -418,6 +419,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="pkb200", choices=["pkb200", "reference"])
     ap.add_argument("--tp-chunks", type=int, default=4)
+    ap.add_argument("--tp-mode", default="nccl", choices=["fused", "nccl"],
+                    help="nccl: chunked GEMM2 + NCCL reduce-scatter/all-gather (default); "
+                         "fused: GEMM2 epilogue stores partials into the owners' buffers over NVLink")
     ap.add_argument("--no-cpu", action="store_true")
     # DRAM bytes per config-5 GEMM1 launch: 1.71 GB measured by ncu at M=4096
     # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).

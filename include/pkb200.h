@@ -83,6 +83,22 @@ int pkb200_fused_matmul_bias_gelu(const void* A, const void* B, const void* bias
 int pkb200_matmul_bias_residual(const void* A, const void* B, const void* bias,
                                 const void* resid, void* out, int M, int N, int K, void* stream);
 
+/* Tensor-parallel GEMM2 that moves its partial sums to their owners itself.
+ * Row block r of this rank's fp32 partial A @ B is stored (plain 16-byte
+ * stores, over NVLink for peers) into slot src_rank of peer_slots[r], an fp32
+ * [world][M/world][N] buffer owned by rank r. After all ranks synchronise, each
+ * owner runs pkb200_reduce_slots_bias_residual on its buffer.
+ * world <= 8; M % world == 0; K, N multiples of 8. New; no reference counterpart. */
+int pkb200_matmul_peer_store_f32(const void* A, const void* B, float* const* peer_slots,
+                                 int world, int src_rank, int M, int N, int K, void* stream);
+
+/* out[rows,N] = bf16(bf16(bf16(sum over the world slots) + bias) + resid), slots
+ * being the [world][rows][N] fp32 buffer filled by pkb200_matmul_peer_store_f32.
+ * New; no reference counterpart. */
+int pkb200_reduce_slots_bias_residual(const float* slots, int world, int rows, int N,
+                                      const void* bias, const void* resid, void* out,
+                                      void* stream);
+
 /* out = bf16(bf16(bf16(Y) + bias) + resid) for an fp32 Y [M,N] (the all-reduced
  * tensor-parallel partial sums). */
 int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
@@ -134,6 +150,13 @@ int pkb200_attention_prefill_kv_append(const void* Q, const void* K_new, const v
                                        void* K_cache, void* V_cache, void* O, int B, int H,
                                        int S_q, int S_cache, int S_max, int D, float scale,
                                        int causal, void* stream);
+
+/* Caps the grid of the persistent tensor-core GEMM at max_ctas CTAs (one per
+ * SM); 0 restores the default of one CTA per SM. Process-wide. The GEMM holds
+ * every SM it is given until it finishes, so a tensor-parallel caller that
+ * wants NCCL kernels to run beside it (overlapping communication) leaves some
+ * SMs free this way. New; no reference counterpart. */
+int pkb200_set_gemm_max_ctas(int max_ctas);
 
 /* Reads (and clears) the device-side error word that bounded waits inside the
  * tensor-core kernels set on timeout (0 = none). Synchronises the device. */

@@ -26,6 +26,8 @@ SIGNATURES = {
                                                     c_float, _P]),
     "pkb200_fused_matmul_bias_gelu": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_matmul_bias_residual": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    "pkb200_matmul_peer_store_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
+    "pkb200_reduce_slots_bias_residual": (c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P]),
     "pkb200_bias_residual_f32": (c_int, [_P, _P, _P, _P, c_int, c_int, _P]),
     "pkb200_matmul_int8": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_mlp_block_workspace_size": (c_size_t, [c_int, c_int, c_int]),
@@ -38,6 +40,7 @@ SIGNATURES = {
     "pkb200_kv_cache_update": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
     "pkb200_attention_prefill_kv_append": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int,
                                                    c_int, c_int, c_int, c_float, c_int, _P]),
+    "pkb200_set_gemm_max_ctas": (c_int, [c_int]),
     "pkb200_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_path_counters": (c_int, [ctypes.POINTER(c_longlong), c_int]),
 }

@@ -34,14 +34,26 @@ enum EpilogueKind : int {
   kEpiBiasResid = 2,  // C = bf16(bf16(bf16(acc) + bias) + resid)       (MLP GEMM2 + residual)
   kEpiColScale = 3,   // C = bf16(acc * scale[n])                       (matmul_int8.cu)
   kEpiF32 = 4,        // C(fp32) = acc   (tensor-parallel partial sums)
+  kEpiPeerStoreF32 = 6,  // owner(m).slot[src_rank][m % rows_per_rank, n] = acc (plain stores;
+                         // the owner sums the slots afterwards)
 };
+
+constexpr int kMaxPeers = 8;
 
 struct EpilogueArgs {
   const __nv_bfloat16* bias;   // [N] or null
   const __nv_bfloat16* resid;  // [M, ld_resid] or null
   const float* col_scale;      // [N] or null
   long long ld_resid;
+  // kEpiPeerStoreF32: rows [r*rows_per_rank, (r+1)*rows_per_rank) of the
+  // product go to peer[r] (an fp32 buffer, possibly on another GPU, reached
+  // through NVLink peer mapping).
+  float* peer[kMaxPeers];
+  long long rows_per_rank;
+  int src_rank;  // kEpiPeerStoreF32: this rank's slot index in every owner's buffer
 };
+
+
 
 // GELU as the golden evaluates it (tests/golden/golden.py:63-66):
 //   z = fp32(x * (1/sqrt 2)); e = fp32(erf(z)) (erf in double, rounded once);
@@ -276,7 +288,13 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
               float a8[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(r[g * 8 + j]);
-              if constexpr (EPI == kEpiF32) {
+              if constexpr (EPI == kEpiPeerStoreF32) {
+                const long long owner = m / ea.rows_per_rank;
+                float* dst = ea.peer[owner] +
+                             (ea.src_rank * ea.rows_per_rank + (m - owner * ea.rows_per_rank)) * N + n;
+                reinterpret_cast<float4*>(dst)[0] = make_float4(a8[0], a8[1], a8[2], a8[3]);
+                reinterpret_cast<float4*>(dst)[1] = make_float4(a8[4], a8[5], a8[6], a8[7]);
+              } else if constexpr (EPI == kEpiF32) {
                 float* cp = static_cast<float*>(C) + m * ldc + n;
                 reinterpret_cast<float4*>(cp)[0] = make_float4(a8[0], a8[1], a8[2], a8[3]);
                 reinterpret_cast<float4*>(cp)[1] = make_float4(a8[4], a8[5], a8[6], a8[7]);

@@ -23,6 +23,9 @@ namespace {
 __device__ int g_device_error;
 
 std::atomic<long long> g_counters[5];
+// Upper bound on the persistent GEMM's grid (0 = one CTA per SM). Lowered by
+// tensor-parallel callers so communication kernels can run beside a GEMM.
+std::atomic<int> g_gemm_max_ctas{0};
 enum { kCntGemmTc = 0, kCntGemmSimt = 1, kCntAttnTc = 2, kCntAttnSimt = 3, kCntOther = 4 };
 
 constexpr int kMaxDevices = 64;
@@ -147,7 +150,10 @@ int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
     attr_set[dev] = true;
   }
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
-  const int grid = tiles < di->sms ? tiles : di->sms;
+  int ctas = di->sms;
+  const int cap = g_gemm_max_ctas.load();
+  if (cap > 0 && cap < ctas) ctas = cap;
+  const int grid = tiles < ctas ? tiles : ctas;
   gemm_tc_kernel<EPI><<<grid, gemm::NUM_THREADS, gemm::SMEM_BYTES, s>>>(
       ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
   g_counters[kCntGemmTc]++;
@@ -366,6 +372,31 @@ __global__ void pkb200_bias_residual_inplace(bf16* y, const bf16* bias, const bf
   }
 }
 
+// out = bf16(bf16(bf16(sum_s slots[s]) + bias) + resid); the W slots are
+// summed in rank order, so the result does not depend on arrival order.
+__global__ void reduce_slots_bias_residual_kernel(const float* __restrict__ slots, int world,
+                                                  long long n, int N,
+                                                  const bf16* __restrict__ bias,
+                                                  const bf16* __restrict__ resid,
+                                                  bf16* __restrict__ out) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n / 4;
+       i += stride) {
+    float4 acc = reinterpret_cast<const float4*>(slots)[i];
+    for (int s = 1; s < world; ++s) {
+      const float4 v = reinterpret_cast<const float4*>(slots + s * n)[i];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+    const long long e0 = i * 4;
+    for (int k = 0; k < 4; ++k) {
+      const int col = static_cast<int>((e0 + k) % N);
+      const float u = bf16_round(bf16_round(a[k]) + __bfloat162float(bias[col]));
+      out[e0 + k] = __float2bfloat16_rn(u + __bfloat162float(resid[e0 + k]));
+    }
+  }
+}
+
 void report(const char* fn, int e) {
   if (e != cudaSuccess)
     std::fprintf(stderr, "[pkb200] %s failed: %s\n", fn,
@@ -454,6 +485,38 @@ int pkb200_matmul_bias_residual(const void* A, const void* B, const void* bias,
   ea.resid = cb(resid);
   ea.ld_resid = N;
   return run_gemm<kEpiBiasResid>(cb(A), cb(B), out, M, N, K, ea, S(stream));
+}
+
+int pkb200_matmul_peer_store_f32(const void* A, const void* B, float* const* peer_slots,
+                                 int world, int src_rank, int M, int N, int K, void* stream) {
+  if (world < 1 || world > kMaxPeers || !peer_slots || src_rank < 0 || src_rank >= world)
+    return cudaErrorInvalidValue;
+  if (M < 0 || M % world) return cudaErrorInvalidValue;
+  EpilogueArgs ea{};
+  for (int r = 0; r < world; ++r) {
+    if (!peer_slots[r] || !aligned16(peer_slots[r])) return cudaErrorInvalidValue;
+    ea.peer[r] = peer_slots[r];
+  }
+  ea.rows_per_rank = M / world;
+  ea.src_rank = src_rank;
+  if (K <= 0 || K % 8 || N % 8 || !aligned16(A) || !aligned16(B)) return cudaErrorInvalidValue;
+  return run_gemm<kEpiPeerStoreF32>(cb(A), cb(B), peer_slots[0], M, N, K, ea, S(stream));
+}
+
+int pkb200_reduce_slots_bias_residual(const float* slots, int world, int rows, int N,
+                                      const void* bias, const void* resid, void* out,
+                                      void* stream) {
+  if (world < 1 || rows < 0 || N < 0) return cudaErrorInvalidValue;
+  if (rows == 0 || N == 0) return cudaSuccess;
+  if (!slots || !bias || !resid || !out || N % 4 || !aligned16(slots)) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  const long long n4 = static_cast<long long>(rows) * N / 4;
+  reduce_slots_bias_residual_kernel<<<grid_for(n4, 256, di), 256, 0, S(stream)>>>(
+      slots, world, static_cast<long long>(rows) * N, N, cb(bias), cb(resid), b(out));
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
 }
 
 int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
@@ -656,6 +719,12 @@ int pkb200_fused_rmsnorm_matmul_noalloc(const void* X, const void* W, const void
   e = run_rmsnorm(cb(X), cb(gamma), ws, M, K, eps, S(stream));
   if (e) return e;
   return run_gemm<kEpiPlain>(ws, cb(W), out, M, N, K, EpilogueArgs{}, S(stream));
+}
+
+int pkb200_set_gemm_max_ctas(int max_ctas) {
+  if (max_ctas < 0) return cudaErrorInvalidValue;
+  g_gemm_max_ctas.store(max_ctas);
+  return cudaSuccess;
 }
 
 int pkb200_device_error(int* code) {

@@ -41,7 +41,7 @@ class TensorParallelMLP:
     """
 
     def __init__(self, gamma, w1_shard, b1_shard, w2_shard, b2, eps=1e-6, group=None, kern=None,
-                 chunks=1):
+                 chunks=1, fused_reduce=False, comm_sms=0):
         if kern is None:
             from . import ops as kern
         self.kern = kern
@@ -51,6 +51,11 @@ class TensorParallelMLP:
         self.chunks = max(1, int(chunks))
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self._comm = None
+        self.fused_reduce = fused_reduce
+        # SMs left free for NCCL while the chunked GEMM2 runs (the persistent GEMM
+        # otherwise holds every SM and the collectives cannot overlap it).
+        self.comm_sms = comm_sms
+        self._symm = None
 
     def _comm_stream(self, x):
         if x.is_cuda and self._comm is None:
@@ -66,6 +71,8 @@ class TensorParallelMLP:
             y32 = k.matmul_f32out(h, self.w2)
             return k.bias_residual_f32(y32, self.b2, x)
         M = h.shape[0]
+        if self.fused_reduce and x.is_cuda:
+            return self._fused(x, h, M)
         if self.chunks == 1 or not x.is_cuda:
             y32 = k.matmul_f32out(h, self.w2)
             dist.all_reduce(y32, group=self.group)
@@ -91,6 +98,10 @@ class TensorParallelMLP:
             raise ValueError(f"M={M} must split into {self.chunks} chunks of a multiple of {W} rows")
         per = rows // W
         keep = []
+        if self.comm_sms:
+            from ._lib import lib
+            sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+            lib().pkb200_set_gemm_max_ctas(max(1, sms - self.comm_sms))
         for i in range(self.chunks):
             lo = i * rows
             y32 = k.matmul_f32out(h[lo:lo + rows], self.w2)
@@ -106,5 +117,47 @@ class TensorParallelMLP:
                 for t in (y32, part, mine):
                     t.record_stream(comm)
             keep.append(y32)
+        if self.comm_sms:
+            from ._lib import lib
+            lib().pkb200_set_gemm_max_ctas(0)
         main.wait_stream(comm)
+        return out
+
+    def _fused(self, x, h, M):
+        """GEMM2 whose epilogue stores each fp32 partial row block straight into
+        its owner's slot buffer over NVLink (pkb200_matmul_peer_store_f32), so
+        the data exchange of the reduce-scatter happens tile by tile inside the
+        GEMM. Each owner then sums its slots in rank order (deterministic) with
+        the bias + residual epilogue on its rows, and an all-gather of the bf16
+        rows rebuilds the output. The slot buffers are torch symmetric memory."""
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from ._lib import check, lib
+        W = self.world
+        rank = dist.get_rank(self.group)
+        d = self.w2.shape[1]
+        if M % W:
+            raise ValueError(f"M={M} is not divisible by the tensor-parallel size {W}")
+        per = M // W
+        if self._symm is None or self._symm[0].shape != (W, per, d):
+            slots = symm_mem.empty(W, per, d, dtype=torch.float32, device=x.device)
+            grp = self.group if self.group is not None else dist.group.WORLD
+            hdl = symm_mem.rendezvous(slots, grp)
+            ptrs = (ctypes.c_void_p * W)(*[int(p) for p in hdl.buffer_ptrs])
+            self._symm = (slots, hdl, ptrs)
+        slots, hdl, ptrs = self._symm
+        stream = torch.cuda.current_stream().cuda_stream
+        hdl.barrier(channel=0)          # every owner has finished reading the previous step
+        check(lib().pkb200_matmul_peer_store_f32(h.data_ptr(), self.w2.data_ptr(), ptrs, W, rank,
+                                                 M, d, h.shape[1], stream),
+              "matmul_peer_store_f32")
+        hdl.barrier(channel=0)          # every rank's partials have landed
+        out = torch.empty_like(x)
+        mine = torch.empty(per, d, dtype=x.dtype, device=x.device)
+        check(lib().pkb200_reduce_slots_bias_residual(
+            slots.data_ptr(), W, per, d, self.b2.data_ptr(), x[rank * per:(rank + 1) * per].data_ptr(),
+            mine.data_ptr(), stream), "reduce_slots_bias_residual")
+        dist.all_gather_into_tensor(out, mine, group=self.group)
         return out
