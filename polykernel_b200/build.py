@@ -17,6 +17,13 @@ def build(verbose: bool = False) -> str:
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True, cwd=CSRC)
+    # the .npy launcher harness (reference cuda_run command line) over the library
+    harness = ["nvcc", "-Wno-deprecated-gpu-targets", "-O2", "-std=c++17", "-o", os.path.join(os.path.dirname(OUT), "cuda_run"),
+               os.path.join(CSRC, "cuda_run.cpp"), "-L" + os.path.dirname(OUT), "-lpkb200",
+               "-lcudart", "-Xlinker", "-rpath=$ORIGIN"]
+    if verbose:
+        print(" ".join(harness))
+    subprocess.run(harness, check=True, cwd=CSRC)
     return OUT
 
 

@@ -1,0 +1,105 @@
+"""The .npy launcher harness (polykernel_b200/_lib/cuda_run), the reference's
+`cuda_run <op> ...` command line (lib/Runtime/cuda_run_main.cpp:356) over this
+library. CPU: usage/exit codes. GPU: ops against the golden fixtures, as the
+reference's tests/kernels/test_cuda_run.py drives its harness."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import golden_np as O
+from tests.helpers import check_attention, check_gate, check_parity
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+EXE = os.path.join(ROOT, "polykernel_b200", "_lib", "cuda_run")
+F = O.from_bits
+
+
+def _exe():
+    if not os.path.exists(EXE):
+        pytest.skip("cuda_run not built")
+    return EXE
+
+
+def _run(*args):
+    return subprocess.run([_exe(), *map(str, args)], capture_output=True, text=True, timeout=300)
+
+
+def _save(path, bits):
+    np.save(path, np.ascontiguousarray(bits, dtype=np.uint16).view("V2"))
+
+
+def _load(path):
+    a = np.load(path)
+    assert a.dtype == np.dtype("V2")
+    return a.view(np.uint16)
+
+
+def test_usage_exit_codes():
+    assert _run().returncode == 2
+    assert _run("no_such_op").returncode == 2
+    assert _run("matmul", "only_one.npy").returncode == 2
+    assert _run("rmsnorm", "a.npy", "b.npy", "--bogus", "1").returncode == 2
+
+
+def test_missing_input_is_runtime_error(tmp_path):
+    r = _run("gelu", tmp_path / "missing.npy", tmp_path / "out.npy")
+    assert r.returncode == 1 and "cannot open" in r.stderr
+
+
+@pytest.mark.gpu
+def test_dev_and_neg(cuda):
+    r = _run("dev")
+    assert r.returncode == 0 and "COMPUTE_CAPABILITY 10.0" in r.stderr
+    r = _run("neg")
+    assert r.returncode == 1 and "PASS" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["sq", "odd", "tiles"])
+def test_gemm_ops_through_harness(golden, cuda, tmp_path, name):
+    g = golden("gemm")
+    for k in ("a", "b", "bias"):
+        _save(tmp_path / f"{k}.npy", g[f"{name}_{k}"])
+    a, b = tmp_path / "a.npy", tmp_path / "b.npy"
+    assert _run("matmul", a, b, tmp_path / "mm.npy").returncode == 0
+    assert _run("fused_rmsnorm_matmul", a, b, tmp_path / "frm.npy").returncode == 0
+    assert _run("fused_matmul_bias_gelu", a, b, tmp_path / "bias.npy",
+                tmp_path / "fbg.npy").returncode == 0
+    af, bf, biasf = (F(g[f"{name}_{k}"]) for k in ("a", "b", "bias"))
+    ref64 = {"mm": O.matmul(af, bf, acc=np.float64),
+             "frm": O.fused_rmsnorm_matmul(af, bf, acc=np.float64),
+             "fbg": O.fused_matmul_bias_gelu(af, bf, biasf, acc=np.float64)}
+    for key in ("mm", "frm", "fbg"):
+        check_parity(F(_load(tmp_path / f"{key}.npy")), F(g[f"{name}_{key}"]), ref64[key])
+
+
+@pytest.mark.gpu
+def test_rmsnorm_gelu_through_harness(golden, cuda, tmp_path):
+    g = golden("elementwise")
+    _save(tmp_path / "x.npy", g["rms_w_x"])
+    _save(tmp_path / "w.npy", g["rms_w_w"])
+    assert _run("rmsnorm", tmp_path / "x.npy", tmp_path / "y.npy", "--weight",
+                tmp_path / "w.npy").returncode == 0
+    check_gate(F(_load(tmp_path / "y.npy")), F(g["rms_w_out"]), min_exact=0.99)
+    _save(tmp_path / "gx.npy", g["gelu_x"])
+    assert _run("gelu", tmp_path / "gx.npy", tmp_path / "gy.npy").returncode == 0
+    check_gate(F(_load(tmp_path / "gy.npy")), F(g["gelu_out"]), min_exact=0.99)
+
+
+@pytest.mark.gpu
+def test_mlp_and_attention_through_harness(golden, cuda, tmp_path):
+    g = golden("mlp")
+    names = ("x", "gamma", "w1", "b1", "w2", "b2")
+    for k in names:
+        _save(tmp_path / f"{k}.npy", g[f"mid_{k}"])
+    assert _run("mlp_block", *[tmp_path / f"{k}.npy" for k in names], tmp_path / "y.npy",
+                "--epsilon", "1e-6").returncode == 0
+    check_parity(F(_load(tmp_path / "y.npy")), F(g["mid_y"]), min_exact=0.98)
+    a = golden("attention")
+    for k in ("q", "k", "v"):
+        _save(tmp_path / f"{k}.npy", a[f"d128_{k}"])
+    assert _run("attention_prefill", tmp_path / "q.npy", tmp_path / "k.npy", tmp_path / "v.npy",
+                tmp_path / "o.npy").returncode == 0
+    check_attention(F(_load(tmp_path / "o.npy")), F(a["d128_o"]))
