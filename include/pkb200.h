@@ -158,6 +158,36 @@ int pkb200_attention_prefill_kv_append(const void* Q, const void* K_new, const v
  * SMs free this way. New; no reference counterpart. */
 int pkb200_set_gemm_max_ctas(int max_ctas);
 
+/* ---- runtime: device detection and the tuning cache (lib/Runtime/
+ * DeviceDetect.cpp:62-69, KernelCache.cpp:83-100 semantics; cache files in
+ * the reference's tuning/schema.json format, version 1). */
+
+/* Writes this device's arch name ("sm_100" on B200). */
+int pkb200_device_arch(char* buf, size_t cap);
+
+/* Loads a tuning-cache JSON file, replacing the current cache. Returns the
+ * number of entries, or -1 with a message in err for an unreadable file or any
+ * schema error (a malformed cache is never silently ignored). Only entries with
+ * validated == true and gpu == this device's arch are ever served. */
+int pkb200_tuning_load(const char* path, char* err, size_t err_cap);
+int pkb200_tuning_clear(void);
+
+/* The tensor-core GEMM config a launch of `op` at (M,N,K) would use, as the
+ * cache's seven `best` fields in schema order (block_m, block_n, block_k,
+ * num_warps, vector_width, unroll, shared_memory_stages). Returns 0 for the
+ * default config, 1 for a cache hit, 2 while a config is forced, -1 for an
+ * unknown op. Ops: matmul, fused_rmsnorm_matmul, fused_matmul_bias_gelu,
+ * matmul_bias_residual, matmul_int8, matmul_f32out, matmul_peer_store_f32. */
+int pkb200_gemm_select(const char* op, int M, int N, int K, int* cfg7);
+
+/* Forces every tensor-core GEMM launch to `cfg7` (for the autotuner); NULL
+ * returns to cache/default selection. cudaErrorInvalidValue for a config with
+ * no compiled variant. */
+int pkb200_set_gemm_config(const int* cfg7);
+
+/* The config of the most recent tensor-core GEMM launch. */
+int pkb200_last_gemm_config(int* cfg7);
+
 /* Reads (and clears) the device-side error word that bounded waits inside the
  * tensor-core kernels set on timeout (0 = none). Synchronises the device. */
 int pkb200_device_error(int* code);

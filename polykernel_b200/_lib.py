@@ -41,6 +41,12 @@ SIGNATURES = {
     "pkb200_attention_prefill_kv_append": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_int, c_int,
                                                    c_int, c_int, c_int, c_float, c_int, _P]),
     "pkb200_set_gemm_max_ctas": (c_int, [c_int]),
+    "pkb200_device_arch": (c_int, [ctypes.c_char_p, c_size_t]),
+    "pkb200_tuning_load": (c_int, [ctypes.c_char_p, ctypes.c_char_p, c_size_t]),
+    "pkb200_tuning_clear": (c_int, []),
+    "pkb200_gemm_select": (c_int, [ctypes.c_char_p, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
+    "pkb200_set_gemm_config": (c_int, [ctypes.POINTER(c_int)]),
+    "pkb200_last_gemm_config": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_path_counters": (c_int, [ctypes.POINTER(c_longlong), c_int]),
 }

@@ -120,19 +120,22 @@ __device__ __forceinline__ uint4 epilogue8(const float (&acc)[8], const Epilogue
 }
 
 namespace gemm {
+// Fixed by the instruction shape and the 128-byte swizzle atom.
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;       // 16 KB
-constexpr int B_BYTES = BK * BN * 2;       // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int B_BLOCK_BYTES = BK * 64 * 2;  // one 64-wide N block: 8 KB
 constexpr int NUM_THREADS = 320;            // 2 control warps + 8 epilogue warps
 constexpr int EPI_THREADS = 256;
-constexpr int TMEM_COLS = 512;             // 2 accumulators x 256 fp32 columns
-constexpr int GROUP_M = 16;                // rasterisation group (L2 reuse)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int GROUP_M = 16;                 // rasterisation group (L2 reuse)
+// Tunable per launch (the tuning cache's block_n / shared_memory_stages):
+// tile width BN in {128, 256} and pipeline depth STAGES.
+constexpr int a_bytes() { return BM * BK * 2; }
+constexpr int b_bytes(int bn) { return BK * bn * 2; }
+constexpr int stage_bytes(int bn) { return a_bytes() + b_bytes(bn); }
+constexpr int smem_bytes(int bn, int stages) {
+  return stages * stage_bytes(bn) + 1024 /*align*/ + 256 /*barriers*/;
+}
+constexpr int tmem_cols(int bn) { return 2 * bn; }  // two accumulators
+constexpr int kMaxSmem = 232448;                    // 227 KB per CTA on sm_100
 }  // namespace gemm
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -145,12 +148,20 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   nb = local / gm;
 }
 
-template <int EPI>
+template <int EPI, int BN, int STAGES>
 __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, void* __restrict__ C, long long ldc,
                    int M, int N, int K, EpilogueArgs ea, int* err) {
-  using namespace gemm;
+  using gemm::BM;
+  using gemm::BK;
+  using gemm::EPI_THREADS;
+  constexpr int A_BYTES = gemm::a_bytes();
+  constexpr int STAGE_BYTES = gemm::stage_bytes(BN);
+  constexpr int B_BLOCK_BYTES = BK * 64 * 2;  // one 64-wide N block
+  constexpr int TMEM_COLS = gemm::tmem_cols(BN);
+  static_assert(BN == 128 || BN == 256, "tile width");
+  static_assert(gemm::smem_bytes(BN, STAGES) <= gemm::kMaxSmem, "pipeline does not fit");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));

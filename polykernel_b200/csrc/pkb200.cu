@@ -7,12 +7,16 @@
 
 #include <atomic>
 #include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
 #include <map>
 #include <mutex>
 #include <utility>
 
 #include "attention_tc.cuh"
 #include "simt_kernels.cuh"
+#include "tuning.h"
 #include "../../include/pkb200.h"
 
 using namespace pkb200;
@@ -120,7 +124,97 @@ int library_workspace(size_t bytes, cudaStream_t s, void** out) {
   return cudaSuccess;
 }
 
+// ------------------------------------------------------------ tuning cache --
+// Runtime side of the tuning cache (lib/Runtime/KernelCache.cpp semantics):
+// entries for this GPU's arch that passed the correctness gate choose the
+// tensor-core GEMM variant for an exact (op, M, N, K) match; anything else
+// runs the default variant. A forced config (set by the autotuner) wins.
+std::vector<tuning::Entry> g_cache;
+bool g_forced = false;
+tuning::Config g_forced_cfg;
+tuning::Config g_last_cfg;
+
+std::string device_arch() {
+  int dev = 0;
+  cudaDeviceProp p{};
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&p, dev) != cudaSuccess)
+    return "unknown";
+  return "sm_" + std::to_string(p.major * 10 + p.minor);
+}
+
+const char* op_name(int epi) {
+  switch (epi) {
+    case kEpiPlain: return "matmul";
+    case kEpiBiasGelu: return "fused_matmul_bias_gelu";
+    case kEpiBiasResid: return "matmul_bias_residual";
+    case kEpiColScale: return "matmul_int8";
+    case kEpiF32: return "matmul_f32out";
+    default: return "matmul_peer_store_f32";
+  }
+}
+
+// The compiled tensor-core GEMM variants, as tuning-cache configs
+// (block_m 128, block_k 64, 10 warps, 16-byte vectors = 8 bf16, 2 TMEM
+// accumulators; block_n and shared_memory_stages vary).
+int variant_of(const tuning::Config& c) {
+  if (c.block_m != gemm::BM || c.block_k != gemm::BK || c.num_warps != gemm::NUM_THREADS / 32 ||
+      c.vector_width != 8 || c.unroll != 2)
+    return -1;
+  if (c.block_n == 256 && c.shared_memory_stages == 4) return 0;
+  if (c.block_n == 256 && c.shared_memory_stages == 3) return 1;
+  if (c.block_n == 128 && c.shared_memory_stages == 4) return 2;
+  if (c.block_n == 128 && c.shared_memory_stages == 6) return 3;
+  return -1;
+}
+
+// source: 0 default, 1 tuning cache, 2 forced.
+tuning::Config select_config(int epi, int M, int N, int K, int* source = nullptr) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (source) *source = 0;
+  if (g_forced) {
+    if (source) *source = 2;
+    return g_forced_cfg;
+  }
+  if (!g_cache.empty()) {
+    const std::string arch = device_arch();
+    const std::string op = op_name(epi);
+    for (const auto& e : g_cache) {
+      const bool op_match = e.op == op || (epi == kEpiPlain && e.op == "fused_rmsnorm_matmul");
+      if (e.validated && e.gpu == arch && op_match && e.M == M && e.N == N && e.K == K &&
+          e.dtype == "bf16" && variant_of(e.best) >= 0) {
+        if (source) *source = 1;
+        return e.best;
+      }
+    }
+  }
+  return tuning::Config{};
+}
+
 // -------------------------------------------------------------------- GEMM --
+template <int EPI, int BN, int STAGES>
+int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N,
+                        int K, const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di) {
+  constexpr int smem = gemm::smem_bytes(BN, STAGES);
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, BN, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + BN - 1) / BN);
+  int ctas = di->sms;
+  const int cap = g_gemm_max_ctas.load();
+  if (cap > 0 && cap < ctas) ctas = cap;
+  const int grid = tiles < ctas ? tiles : ctas;
+  gemm_tc_kernel<EPI, BN, STAGES><<<grid, gemm::NUM_THREADS, smem, s>>>(
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
+  g_counters[kCntGemmTc]++;
+  return cudaGetLastError();
+}
+
 template <int EPI>
 int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
                    const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di) {
@@ -139,25 +233,17 @@ int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
     if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, dims, str, box))
       return cudaErrorInvalidValue;
   }
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         gemm::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  const tuning::Config cfg = select_config(EPI, M, N, K);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_last_cfg = cfg;
   }
-  const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
-  int ctas = di->sms;
-  const int cap = g_gemm_max_ctas.load();
-  if (cap > 0 && cap < ctas) ctas = cap;
-  const int grid = tiles < ctas ? tiles : ctas;
-  gemm_tc_kernel<EPI><<<grid, gemm::NUM_THREADS, gemm::SMEM_BYTES, s>>>(
-      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
-  g_counters[kCntGemmTc]++;
-  return cudaGetLastError();
+  switch (variant_of(cfg)) {
+    case 1: return launch_gemm_variant<EPI, 256, 3>(ma, mb, C, M, N, K, ea, s, di);
+    case 2: return launch_gemm_variant<EPI, 128, 4>(ma, mb, C, M, N, K, ea, s, di);
+    case 3: return launch_gemm_variant<EPI, 128, 6>(ma, mb, C, M, N, K, ea, s, di);
+    default: return launch_gemm_variant<EPI, 256, 4>(ma, mb, C, M, N, K, ea, s, di);
+  }
 }
 
 template <int EPI, typename TB>
@@ -724,6 +810,85 @@ int pkb200_fused_rmsnorm_matmul_noalloc(const void* X, const void* W, const void
 int pkb200_set_gemm_max_ctas(int max_ctas) {
   if (max_ctas < 0) return cudaErrorInvalidValue;
   g_gemm_max_ctas.store(max_ctas);
+  return cudaSuccess;
+}
+
+int pkb200_device_arch(char* buf, size_t cap) {
+  const std::string a = device_arch();
+  if (!buf || cap == 0) return cudaErrorInvalidValue;
+  std::snprintf(buf, cap, "%s", a.c_str());
+  return a == "unknown" ? cudaErrorNoDevice : cudaSuccess;
+}
+
+int pkb200_tuning_load(const char* path, char* err, size_t err_cap) {
+  auto set_err = [&](const std::string& m) {
+    if (err && err_cap) std::snprintf(err, err_cap, "%s", m.c_str());
+  };
+  if (!path) {
+    set_err("null path");
+    return -1;
+  }
+  std::ifstream f(path);
+  if (!f) {
+    set_err(std::string("cannot open ") + path);
+    return -1;
+  }
+  std::stringstream ss;
+  ss << f.rdbuf();
+  std::vector<tuning::Entry> entries;
+  std::string msg;
+  if (!tuning::parse_cache(ss.str(), entries, msg)) {
+    set_err(msg);
+    return -1;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_cache = entries;
+  set_err("");
+  return static_cast<int>(entries.size());
+}
+
+int pkb200_tuning_clear(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_cache.clear();
+  return cudaSuccess;
+}
+
+static void cfg_out(const tuning::Config& c, int* cfg7) {
+  const int v[7] = {c.block_m, c.block_n, c.block_k, c.num_warps, c.vector_width, c.unroll,
+                    c.shared_memory_stages};
+  for (int i = 0; i < 7; ++i) cfg7[i] = v[i];
+}
+
+int pkb200_gemm_select(const char* op, int M, int N, int K, int* cfg7) {
+  if (!op || !cfg7) return -1;
+  int epi = -1;
+  for (int e = kEpiPlain; e <= kEpiPeerStoreF32; ++e)
+    if (std::strcmp(op, op_name(e)) == 0) epi = e;
+  if (std::strcmp(op, "fused_rmsnorm_matmul") == 0) epi = kEpiPlain;
+  if (epi < 0) return -1;
+  int source = 0;
+  const tuning::Config c = select_config(epi, M, N, K, &source);
+  cfg_out(c, cfg7);
+  return source;
+}
+
+int pkb200_set_gemm_config(const int* cfg7) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!cfg7) {
+    g_forced = false;
+    return cudaSuccess;
+  }
+  tuning::Config c{cfg7[0], cfg7[1], cfg7[2], cfg7[3], cfg7[4], cfg7[5], cfg7[6]};
+  if (variant_of(c) < 0) return cudaErrorInvalidValue;
+  g_forced = true;
+  g_forced_cfg = c;
+  return cudaSuccess;
+}
+
+int pkb200_last_gemm_config(int* cfg7) {
+  if (!cfg7) return cudaErrorInvalidValue;
+  std::lock_guard<std::mutex> lk(g_mu);
+  cfg_out(g_last_cfg, cfg7);
   return cudaSuccess;
 }
 

@@ -1,0 +1,252 @@
+"""Tuning cache and autotuner for the tensor-core GEMM (the reference's
+lib/Autotune + lib/Runtime/KernelCache, re-done around tcgen05 tile shapes).
+
+* `ConfigSpace` enumerates tcgen05 GEMM configs (tile width block_n and pipeline
+  depth shared_memory_stages; block_m, block_k, warps, vector width and TMEM
+  accumulator count are fixed by the kernel) and prunes those that do not fit
+  shared memory (227 KB per CTA) or TMEM (512 columns), like ConfigSpace's prune
+  rules (lib/Autotune/ConfigSpace.cpp:44-142). Only configs with a compiled
+  variant survive.
+* `autotune` times every surviving config on the GPU, gates each on
+  correctness (bit-identical to the default variant -- the K reduction order does
+  not depend on the tile width or depth -- and cosine / max_rel_err / PCC
+  against an fp32 torch reference of the same product), and picks the fastest
+  validated one (Benchmark.cpp:31-52 semantics: an unvalidated config is never
+  selected).
+* `load` / `save` / `validate` read and write cache files in the reference's
+  format (tuning/schema.json, version 1; restated in tuning_schema.json here).
+  The C runtime (`pkb200_tuning_load`) parses the same files with the same rules.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+
+SCHEMA_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tuning_schema.json")
+CONFIG_FIELDS = ("block_m", "block_n", "block_k", "num_warps", "vector_width", "unroll",
+                 "shared_memory_stages")
+SMEM_LIMIT = 232448          # bytes per CTA on sm_100
+TMEM_COLUMNS = 512
+COMPILED = {(256, 4), (256, 3), (128, 4), (128, 6)}   # (block_n, stages) with a kernel
+DEFAULT = dict(block_m=128, block_n=256, block_k=64, num_warps=10, vector_width=8, unroll=2,
+               shared_memory_stages=4)
+
+
+class SchemaError(ValueError):
+    pass
+
+
+# ------------------------------------------------------------ config space --
+class ConfigSpace:
+    """tcgen05 GEMM configs: block_n x stages over the kernel's fixed axes."""
+    block_n = (64, 128, 256)
+    stages = (2, 3, 4, 5, 6, 7, 8)
+
+    @staticmethod
+    def smem_bytes(c):
+        stage = c["block_m"] * c["block_k"] * 2 + c["block_k"] * c["block_n"] * 2
+        return c["shared_memory_stages"] * stage + 1024 + 256
+
+    @classmethod
+    def prune_reason(cls, c):
+        if cls.smem_bytes(c) > SMEM_LIMIT:
+            return "shared memory"
+        if c["unroll"] * c["block_n"] > TMEM_COLUMNS:
+            return "tmem columns"
+        if (c["block_n"], c["shared_memory_stages"]) not in COMPILED:
+            return "no compiled variant"
+        return None
+
+    @classmethod
+    def enumerate(cls, limit=None):
+        out = []
+        for bn in cls.block_n:
+            for st in cls.stages:
+                c = dict(DEFAULT, block_n=bn, shared_memory_stages=st)
+                if cls.prune_reason(c) is None:
+                    out.append(c)
+        return out[:limit] if limit else out
+
+
+# ----------------------------------------------------------------- schema --
+def _check_keys(obj, keys, where):
+    if not isinstance(obj, dict):
+        raise SchemaError(f"{where}: expected an object")
+    extra = set(obj) - set(keys)
+    if extra:
+        raise SchemaError(f"{where}: unknown field '{sorted(extra)[0]}'")
+    missing = [k for k in keys if k not in obj]
+    if missing:
+        raise SchemaError(f"{where}: missing field '{missing[0]}'")
+
+
+def _is_int(v):
+    return isinstance(v, int) and not isinstance(v, bool)
+
+
+def _is_num(v):
+    return isinstance(v, (int, float)) and not isinstance(v, bool)
+
+
+def validate(doc):
+    """Raise SchemaError unless `doc` is a valid version-1 cache document."""
+    _check_keys(doc, ("version", "entries"), "cache")
+    if not _is_int(doc["version"]) or doc["version"] != 1:
+        raise SchemaError(f"cache.version: unsupported version {doc['version']!r} (expected 1)")
+    if not isinstance(doc["entries"], list):
+        raise SchemaError("cache.entries: expected an array")
+    for i, e in enumerate(doc["entries"]):
+        w = f"entries[{i}]"
+        _check_keys(e, ("gpu", "op", "shape", "best", "scored_by", "time_ms", "validated",
+                        "correctness"), w)
+        for k in ("gpu", "op"):
+            if not isinstance(e[k], str):
+                raise SchemaError(f"{w}.{k}: expected a string")
+        _check_keys(e["shape"], ("M", "N", "K", "dtype"), w + ".shape")
+        for k in ("M", "N", "K"):
+            if not _is_int(e["shape"][k]):
+                raise SchemaError(f"{w}.shape.{k}: expected an integer")
+        if not isinstance(e["shape"]["dtype"], str):
+            raise SchemaError(f"{w}.shape.dtype: expected a string")
+        _check_keys(e["best"], CONFIG_FIELDS, w + ".best")
+        for k in CONFIG_FIELDS:
+            if not _is_int(e["best"][k]):
+                raise SchemaError(f"{w}.best.{k}: expected an integer")
+        if e["scored_by"] not in ("measure", "compile_time_model"):
+            raise SchemaError(f"{w}.scored_by: must be measure or compile_time_model")
+        if e["time_ms"] is not None and not _is_num(e["time_ms"]):
+            raise SchemaError(f"{w}.time_ms: expected a number or null")
+        if (e["time_ms"] is None) != (e["scored_by"] == "compile_time_model"):
+            raise SchemaError(f"{w}.time_ms: null iff scored_by is compile_time_model")
+        if not isinstance(e["validated"], bool):
+            raise SchemaError(f"{w}.validated: expected a boolean")
+        _check_keys(e["correctness"], ("cosine", "max_rel_err", "pcc"), w + ".correctness")
+        for k in ("cosine", "max_rel_err", "pcc"):
+            if not _is_num(e["correctness"][k]):
+                raise SchemaError(f"{w}.correctness.{k}: expected a number")
+    return doc
+
+
+def load(path):
+    with open(path) as f:
+        return validate(json.load(f))
+
+
+def save(doc, path):
+    validate(doc)
+    with open(path, "w") as f:
+        json.dump(doc, f, indent=2)
+        f.write("\n")
+
+
+def entry(gpu, op, M, N, K, best, time_ms, validated, correctness, dtype="bf16"):
+    return {"gpu": gpu, "op": op, "shape": {"M": M, "N": N, "K": K, "dtype": dtype},
+            "best": {k: int(best[k]) for k in CONFIG_FIELDS},
+            "scored_by": "measure" if time_ms is not None else "compile_time_model",
+            "time_ms": time_ms, "validated": bool(validated),
+            "correctness": {k: float(correctness[k]) for k in ("cosine", "max_rel_err", "pcc")}}
+
+
+def merge(doc, new_entries):
+    """Replace entries with the same (gpu, op, shape) key, append the rest."""
+    key = lambda e: (e["gpu"], e["op"], e["shape"]["M"], e["shape"]["N"], e["shape"]["K"],  # noqa
+                     e["shape"]["dtype"])
+    keep = {key(e): e for e in doc.get("entries", [])}
+    for e in new_entries:
+        keep[key(e)] = e
+    return {"version": 1, "entries": list(keep.values())}
+
+
+# --------------------------------------------------------- runtime access --
+def _cfg_array(c):
+    return (ctypes.c_int * 7)(*[int(c[k]) for k in CONFIG_FIELDS])
+
+
+def runtime_load(path):
+    """Load a cache file into the C runtime; returns the entry count."""
+    from ._lib import lib
+    err = ctypes.create_string_buffer(512)
+    n = lib().pkb200_tuning_load(path.encode(), err, 512)
+    if n < 0:
+        raise SchemaError(err.value.decode())
+    return n
+
+
+def runtime_select(op, M, N, K):
+    """(source, config) the runtime would use: source 0 default, 1 cache, 2 forced."""
+    from ._lib import lib
+    out = (ctypes.c_int * 7)()
+    src = lib().pkb200_gemm_select(op.encode(), M, N, K, out)
+    if src < 0:
+        raise ValueError(f"unknown op {op!r}")
+    return src, dict(zip(CONFIG_FIELDS, list(out)))
+
+
+def device_arch():
+    from ._lib import lib
+    buf = ctypes.create_string_buffer(32)
+    lib().pkb200_device_arch(buf, 32)
+    return buf.value.decode()
+
+
+# --------------------------------------------------------------- autotune --
+def _metrics(a, r):
+    import torch
+    a = a.double().flatten()
+    r = r.double().flatten()
+    cos = float(torch.dot(a, r) / (a.norm() * r.norm()).clamp_min(1e-300))
+    rel = float(((a - r).abs() / (r.abs() + 1e-6)).max())
+    ac, rc = a - a.mean(), r - r.mean()
+    pcc = float((ac * rc).sum() / (ac.norm() * rc.norm()).clamp_min(1e-300))
+    return {"cosine": cos, "max_rel_err": rel, "pcc": pcc}
+
+
+def autotune(op, M, N, K, iters=10, warmup=3, seed=0):
+    """Time every ConfigSpace config for `op` at (M, N, K) on the current GPU and
+    return cache entries (one per op/shape: the fastest validated config).
+    Ops: matmul, fused_matmul_bias_gelu, matmul_bias_residual."""
+    import torch
+
+    from . import ops
+    from ._lib import lib
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    b = (torch.randn(K, N, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    bias = (0.02 * torch.randn(N, device="cuda", generator=g)).to(torch.bfloat16)
+    resid = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16)
+    run = {"matmul": lambda: ops.matmul(a, b),
+           "fused_matmul_bias_gelu": lambda: ops.fused_matmul_bias_gelu(a, b, bias),
+           "matmul_bias_residual": lambda: ops.matmul_bias_residual(a, b, bias, resid)}[op]
+    ref32 = a.float() @ b.float()
+    if op == "fused_matmul_bias_gelu":
+        ref32 = torch.nn.functional.gelu(ref32 + bias.float())
+    elif op == "matmul_bias_residual":
+        ref32 = ref32 + bias.float() + resid.float()
+    results = []
+    try:
+        lib().pkb200_set_gemm_config(_cfg_array(DEFAULT))
+        base = run()
+        for cfg in ConfigSpace.enumerate():
+            if lib().pkb200_set_gemm_config(_cfg_array(cfg)) != 0:
+                continue
+            out = run()
+            torch.cuda.synchronize()
+            m = _metrics(out.float(), ref32)
+            ok = bool(torch.equal(out, base)) and m["cosine"] >= 0.999 and m["pcc"] >= 0.99
+            for _ in range(warmup):
+                run()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(iters):
+                run()
+            e.record()
+            torch.cuda.synchronize()
+            results.append((s.elapsed_time(e) / iters, ok, cfg, m))
+    finally:
+        lib().pkb200_set_gemm_config(None)
+    valid = [r for r in results if r[1]]
+    if not valid:
+        return []
+    t, _, cfg, m = min(valid, key=lambda r: r[0])
+    return [entry(device_arch(), op, M, N, K, cfg, t, True, m)]
