@@ -38,7 +38,7 @@ struct Npy {
 };
 
 int elem_size(const std::string& d) {
-  if (d == "<V2" || d == "<u2" || d == "<i2") return 2;
+  if (d == "<V2" || d == "|V2" || d == "<u2" || d == "<i2") return 2;
   if (d == "|i1" || d == "<i1" || d == "|u1") return 1;
   if (d == "<f4") return 4;
   throw std::runtime_error("unsupported npy descr " + d);
@@ -83,8 +83,10 @@ Npy read_npy(const std::string& path, const char* want_descr) {
     a.shape.push_back(std::stoll(dims.substr(pos, e - pos)));
     pos = e;
   }
-  if (want_descr && a.descr != want_descr &&
-      !(std::string(want_descr) == "|i1" && a.descr == "<i1"))
+  const std::string want = want_descr ? want_descr : "";
+  const bool same = a.descr == want || (want == "|i1" && a.descr == "<i1") ||
+                    (want == "<V2" && a.descr == "|V2");  // NumPy writes 2-byte voids as |V2
+  if (want_descr && !same)
     throw std::runtime_error(path + ": dtype " + a.descr + ", expected " + want_descr);
   a.bytes.resize(static_cast<size_t>(a.size()) * elem_size(a.descr));
   f.read(a.bytes.data(), static_cast<std::streamsize>(a.bytes.size()));
