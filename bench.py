@@ -163,7 +163,7 @@ class ClockSampler:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -319,23 +319,41 @@ def run_gpu_arm(args):
     attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ea)
 
     # End to end through the public API with HOST buffers: pinned host X/Q/K/V
-    # in, this rank's Y rows and O out, every step.
+    # in, this rank's Y rows and O out, every step. The MLP streams row chunks
+    # (polykernel_b200.streaming.HostStreamed) so the copies overlap compute.
+    from polykernel_b200.streaming import HostStreamed
     xh = x.cpu().pin_memory()
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, kn, vn))
-    r_lo, r_hi = (M * rank) // world, (M * (rank + 1)) // world
-    yh = torch.empty(r_hi - r_lo, d, dtype=bf).pin_memory()
+    yh = torch.empty(M, d, dtype=bf).pin_memory()
     oh = torch.empty_like(o, device="cpu").pin_memory()
-    xd, qd, kd, vd = (torch.empty_like(t) for t in (x, q, kn, vn))
+    qd, kd, vd = (torch.empty_like(t) for t in (q, kn, vn))
+    if world == 1:
+        ws_c = ops.mlp_workspace(-(-M // args.e2e_chunks), d, ffn, dev)
+        fwd = lambda xx, out: ops.mlp_block(xx, gamma, w1, b1, w2, b2, eps, ws_c, out)  # noqa
+    else:
+        fwd = lambda xx, out: out.copy_(tpm(xx))  # noqa
+    streamer = HostStreamed(fwd, chunks=args.e2e_chunks)
+    r_lo, r_hi = (M * rank) // world, (M * (rank + 1)) // world
 
     def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        mlp(xd, y)
+        streamer(xh, yh, dev)
+        s_in, s_out = streamer.copy_streams
+        with torch.cuda.stream(s_in):
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+        stream.wait_event(ev)
         ops.attention_prefill_kv_append(qd, kd, vd, kc, vc, 0, True, out=o)
-        yh.copy_(y[r_lo:r_hi], non_blocking=True)
-        oh.copy_(o, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            oh.copy_(o, non_blocking=True)
+            ev2 = torch.cuda.Event()
+            ev2.record(s_out)
+        stream.wait_event(ev2)
 
     e2e_step()
     barrier()
@@ -348,7 +366,10 @@ def run_gpu_arm(args):
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     h2d = (xh.numel() + qh.numel() + kh.numel() + vh.numel()) * 2
+    # every rank copies the full Y back (it holds it after the all-gather); only
+    # this rank's rows are new information, but all bytes cross PCIe
     d2h = (yh.numel() + oh.numel()) * 2
+    del r_lo, r_hi
 
     def gmax(v):
         if world == 1:
@@ -415,13 +436,15 @@ def run_gpu_arm(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="pkb200", choices=["pkb200", "reference"])
     ap.add_argument("--tp-chunks", type=int, default=4)
     ap.add_argument("--tp-mode", default="nccl", choices=["fused", "nccl"],
                     help="nccl: chunked GEMM2 + NCCL reduce-scatter/all-gather (default); "
                          "fused: GEMM2 epilogue stores partials into the owners' buffers over NVLink")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="row chunks of the host-streamed end-to-end MLP")
     ap.add_argument("--no-cpu", action="store_true")
     # DRAM bytes per config-5 GEMM1 launch: 1.71 GB measured by ncu at M=4096
     # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).

@@ -188,6 +188,13 @@ int pkb200_set_gemm_config(const int* cfg7);
 /* The config of the most recent tensor-core GEMM launch. */
 int pkb200_last_gemm_config(int* cfg7);
 
+/* Failure-detection self test: launches one warp that waits on an mbarrier
+ * nothing will complete, with a wait limit of limit_cycles SM clocks (at most
+ * the kernels' own ~2 s limit). The bounded wait gives up, the kernel returns
+ * normally and *code receives the error word it recorded (6 = self-test
+ * timeout); the CUDA context stays usable. New; no reference counterpart. */
+int pkb200_selftest_wait_timeout(long long limit_cycles, int* code);
+
 /* Reads (and clears) the device-side error word that bounded waits inside the
  * tensor-core kernels set on timeout (0 = none). Synchronises the device. */
 int pkb200_device_error(int* code);

@@ -47,6 +47,7 @@ SIGNATURES = {
     "pkb200_gemm_select": (c_int, [ctypes.c_char_p, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
     "pkb200_set_gemm_config": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_last_gemm_config": (c_int, [ctypes.POINTER(c_int)]),
+    "pkb200_selftest_wait_timeout": (c_int, [c_longlong, ctypes.POINTER(c_int)]),
     "pkb200_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_path_counters": (c_int, [ctypes.POINTER(c_longlong), c_int]),
 }

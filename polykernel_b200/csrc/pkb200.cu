@@ -483,6 +483,22 @@ __global__ void reduce_slots_bias_residual_kernel(const float* __restrict__ slot
   }
 }
 
+// Self test of the bounded waits: one warp waits on an mbarrier nobody
+// arrives on, with a short limit. The wait gives up, records its code in the
+// error word and the kernel returns normally -- no hang, no fault.
+__global__ void wait_timeout_selftest_kernel(int* err, long long limit, int* gave_up) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, err, &abort_flag, kErrTimeoutSelfTest, limit);
+  if (threadIdx.x == 0) *gave_up = ok ? 0 : 1;
+}
+
 void report(const char* fn, int e) {
   if (e != cudaSuccess)
     std::fprintf(stderr, "[pkb200] %s failed: %s\n", fn,
@@ -890,6 +906,29 @@ int pkb200_last_gemm_config(int* cfg7) {
   std::lock_guard<std::mutex> lk(g_mu);
   cfg_out(g_last_cfg, cfg7);
   return cudaSuccess;
+}
+
+int pkb200_selftest_wait_timeout(long long limit_cycles, int* code) {
+  if (limit_cycles <= 0 || limit_cycles > kSpinLimitCycles || !code) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  // clear any earlier code, run the wait, read what it recorded
+  int dummy = 0;
+  e = pkb200_device_error(&dummy);
+  if (e) return e;
+  int* flag = nullptr;
+  e = cudaMalloc(&flag, sizeof(int));
+  if (e) return e;
+  wait_timeout_selftest_kernel<<<1, 32>>>(di->err, limit_cycles, flag);
+  e = cudaGetLastError();
+  int gave_up = 0;
+  if (!e) e = cudaMemcpy(&gave_up, flag, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(flag);
+  if (e) return e;
+  e = pkb200_device_error(code);
+  if (!e && !gave_up) *code = 0;
+  return e;
 }
 
 int pkb200_device_error(int* code) {

@@ -27,6 +27,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 3,  // epilogue waited too long for a finished accumulator
   kErrTimeoutSoftmax = 4,   // attention softmax warps waited too long
   kErrAbortSeen = 5,        // a role saw another role's abort
+  kErrTimeoutSelfTest = 6,  // the wait-timeout self test (a wait nobody satisfies)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -71,13 +72,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // recording `code` in *err and raising *abort) if the limit runs out or if
 // another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
-                                          volatile int* abort_flag, int code) {
+                                          volatile int* abort_flag, int code,
+                                          long long limit = kSpinLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kSpinLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(err, 0, code);
       *abort_flag = 1;
       return false;
