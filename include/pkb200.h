@@ -195,6 +195,18 @@ int pkb200_last_gemm_config(int* cfg7);
  * timeout); the CUDA context stays usable. New; no reference counterpart. */
 int pkb200_selftest_wait_timeout(long long limit_cycles, int* code);
 
+/* ---- serving engine ABI. The reference's Modal app binds
+ *   int polykernel_fused_mlp_block(float* in, float* out, int M, int N, int K)
+ * through ctypes (modal/app.py:206-215, 795, 836) but no library in the
+ * reference implements it. Here: pkb200_engine_load_mlp copies one MLP block's
+ * bf16 weights (host pointers; gamma may be NULL) to the current device; then
+ * polykernel_fused_mlp_block runs that block on host fp32 rows: in [M,K] and
+ * out [M,N] with K == N == d, rounded to bf16 on the way in (RNE) and widened
+ * on the way out. Returns 0, 2 if no weights are loaded, or a cudaError_t. */
+int pkb200_engine_load_mlp(const void* gamma, const void* w1, const void* b1, const void* w2,
+                           const void* b2, int d, int ffn, float eps);
+int polykernel_fused_mlp_block(float* in, float* out, int M, int N, int K);
+
 /* Reads (and clears) the device-side error word that bounded waits inside the
  * tensor-core kernels set on timeout (0 = none). Synchronises the device. */
 int pkb200_device_error(int* code);

@@ -48,6 +48,8 @@ SIGNATURES = {
     "pkb200_set_gemm_config": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_last_gemm_config": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_selftest_wait_timeout": (c_int, [c_longlong, ctypes.POINTER(c_int)]),
+    "pkb200_engine_load_mlp": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_float]),
+    "polykernel_fused_mlp_block": (c_int, [_P, _P, c_int, c_int, c_int]),
     "pkb200_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_path_counters": (c_int, [ctypes.POINTER(c_longlong), c_int]),
 }

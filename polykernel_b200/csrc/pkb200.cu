@@ -499,6 +499,32 @@ __global__ void wait_timeout_selftest_kernel(int* err, long long limit, int* gav
   if (threadIdx.x == 0) *gave_up = ok ? 0 : 1;
 }
 
+// fp32 <-> bf16 conversion for the engine entry point (RNE, as the golden).
+__global__ void f32_to_bf16_kernel(const float* __restrict__ in, bf16* __restrict__ out,
+                                   long long n) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride)
+    out[i] = __float2bfloat16_rn(in[i]);
+}
+__global__ void bf16_to_f32_kernel(const bf16* __restrict__ in, float* __restrict__ out,
+                                   long long n) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride)
+    out[i] = __bfloat162float(in[i]);
+}
+
+// The serving engine's resident MLP weights (one set per process, on the
+// device that loaded them).
+struct EngineMlp {
+  bool loaded = false;
+  int device = -1, d = 0, ffn = 0;
+  float eps = 1e-6f;
+  bf16 *gamma = nullptr, *w1 = nullptr, *b1 = nullptr, *w2 = nullptr, *b2 = nullptr;
+};
+EngineMlp g_engine;
+
 void report(const char* fn, int e) {
   if (e != cudaSuccess)
     std::fprintf(stderr, "[pkb200] %s failed: %s\n", fn,
@@ -929,6 +955,80 @@ int pkb200_selftest_wait_timeout(long long limit_cycles, int* code) {
   e = pkb200_device_error(code);
   if (!e && !gave_up) *code = 0;
   return e;
+}
+
+int pkb200_engine_load_mlp(const void* gamma, const void* w1, const void* b1, const void* w2,
+                           const void* b2, int d, int ffn, float eps) {
+  if (!w1 || !b1 || !w2 || !b2 || d <= 0 || ffn <= 0) return cudaErrorInvalidValue;
+  std::lock_guard<std::mutex> lk(g_mu);
+  EngineMlp e;
+  cudaError_t st = cudaGetDevice(&e.device);
+  if (st) return st;
+  e.d = d;
+  e.ffn = ffn;
+  e.eps = eps;
+  const size_t sizes[5] = {static_cast<size_t>(d), static_cast<size_t>(d) * ffn,
+                           static_cast<size_t>(ffn), static_cast<size_t>(ffn) * d,
+                           static_cast<size_t>(d)};
+  const void* src[5] = {gamma, w1, b1, w2, b2};
+  bf16** dst[5] = {&e.gamma, &e.w1, &e.b1, &e.w2, &e.b2};
+  for (int i = 0; i < 5; ++i) {
+    if (!src[i]) continue;  // gamma may be null (no scale)
+    st = cudaMalloc(reinterpret_cast<void**>(dst[i]), sizes[i] * 2);
+    if (!st) st = cudaMemcpy(*dst[i], src[i], sizes[i] * 2, cudaMemcpyHostToDevice);
+    if (st) {
+      for (int k = 0; k <= i; ++k) cudaFree(*dst[k]);
+      return st;
+    }
+  }
+  for (bf16* ptr : {g_engine.gamma, g_engine.w1, g_engine.b1, g_engine.w2, g_engine.b2})
+    if (ptr) cudaFree(ptr);
+  e.loaded = true;
+  g_engine = e;
+  return cudaSuccess;
+}
+
+int polykernel_fused_mlp_block(float* in, float* out, int M, int N, int K) {
+  EngineMlp e;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    e = g_engine;
+  }
+  if (!e.loaded) return 2;                         // no weights loaded
+  if (!in || !out || M < 0 || K != e.d || N != e.d) return cudaErrorInvalidValue;
+  if (M == 0) return cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != e.device) return cudaErrorInvalidDevice;
+  DeviceInfo* di = nullptr;
+  int st = current_device_info(&di);
+  if (st) return st;
+  const size_t n_in = static_cast<size_t>(M) * K;
+  const size_t ws_bytes = pkb200_mlp_block_workspace_size(M, e.d, e.ffn);
+  float* f32 = nullptr;
+  bf16 *x = nullptr, *y = nullptr;
+  void* ws = nullptr;
+  st = cudaMalloc(&f32, n_in * 4);
+  if (!st) st = cudaMalloc(&x, n_in * 2);
+  if (!st) st = cudaMalloc(&y, n_in * 2);
+  if (!st) st = cudaMalloc(&ws, ws_bytes);
+  if (!st) st = cudaMemcpy(f32, in, n_in * 4, cudaMemcpyHostToDevice);
+  if (!st) {
+    f32_to_bf16_kernel<<<grid_for(static_cast<long long>(n_in), 256, di), 256>>>(f32, x, n_in);
+    st = cudaGetLastError();
+  }
+  if (!st) st = pkb200_mlp_block(x, e.gamma, e.w1, e.b1, e.w2, e.b2, y, M, e.d, e.ffn, e.eps, ws,
+                                 ws_bytes, nullptr);
+  if (!st) {
+    bf16_to_f32_kernel<<<grid_for(static_cast<long long>(n_in), 256, di), 256>>>(y, f32, n_in);
+    st = cudaGetLastError();
+  }
+  if (!st) st = cudaMemcpy(out, f32, n_in * 4, cudaMemcpyDeviceToHost);
+  cudaFree(f32);
+  cudaFree(x);
+  cudaFree(y);
+  cudaFree(ws);
+  return st;
 }
 
 int pkb200_device_error(int* code) {

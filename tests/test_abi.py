@@ -13,7 +13,7 @@ HEADER = os.path.join(ROOT, "include", "pkb200.h")
 
 def _declared():
     txt = open(HEADER).read()
-    c_names = sorted(set(re.findall(r"\b(pkb200_\w+)\s*\(", txt)))
+    c_names = sorted(set(re.findall(r"\b(pkb200_\w+|polykernel_\w+)\s*\(", txt)))
     cpp_names = sorted(set(re.findall(r"^void (launch_\w+)\(", txt, flags=re.M)))
     return c_names, cpp_names
 
