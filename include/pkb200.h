@@ -104,6 +104,23 @@ int pkb200_reduce_slots_bias_residual(const float* slots, int world, int rows, i
 int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
                              int M, int N, void* stream);
 
+/* out = rmsnorm(bf16(x + resid); weight, eps) over the last axis
+ * (golden.fused_residual_rmsnorm, tests/golden/golden.py:108-112): the residual
+ * add + next-layer norm that follows the MLP. sum_out (nullable) receives the
+ * rounded sum, the new residual stream. New entry point (the reference has the
+ * fusion pass FuseResidualRmsnorm but no kernel for it). */
+int pkb200_fused_residual_rmsnorm(const void* x, const void* resid, const void* weight,
+                                  void* out, void* sum_out, int rows, int cols, float eps,
+                                  void* stream);
+
+/* [Q|K|V] = X @ W_qkv (golden.qkv_projection, golden.py:120-136) with the
+ * split and head reshape done in the GEMM epilogue: X [B*S, H*Dh], W_qkv
+ * [H*Dh, 3*H*Dh]; Q, K, V are written in the [B, H, S, Dh] layout the attention
+ * entry points take (the golden returns [B, S, H, Dh]; same values). Dh % 8 == 0.
+ * New entry point. */
+int pkb200_qkv_projection(const void* X, const void* W_qkv, void* Q, void* K, void* V, int B,
+                          int S, int H, int Dh, void* stream);
+
 /* C = bf16(A @ (Wq * scale[n])); A bf16 [M,K], Wq int8 [K,N], scale fp32 [N].
  * Replaces launch_matmul_int8 (kernels/generated/matmul_int8.cu:97-98). */
 int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void* C, int M,

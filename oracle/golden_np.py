@@ -163,3 +163,19 @@ def attention_prefill_kv_append(q, k_new, v_new, k_cache, v_cache, s_cache, caus
     vc[:, :, s_cache:s_cache + Sq] = bf16(v_new)
     o = attention_prefill(q, kc[:, :, :s_cache + Sq], vc[:, :, :s_cache + Sq], causal, scale)
     return o, kc, vc
+
+
+# --------------------------------------------------- next-row fragments --
+def fused_residual_rmsnorm(x, residual, weight=None, eps=1e-5):
+    """golden.fused_residual_rmsnorm (golden.py:108-112): rmsnorm(add(x, residual))."""
+    return rmsnorm(add(x, residual), weight, eps)
+
+
+def qkv_projection(x, w_qkv, num_heads):
+    """golden.qkv_projection (golden.py:120-136): x @ w_qkv (bf16), split the last
+    axis into Q, K, V and reshape each to [..., num_heads, head_dim]."""
+    proj = matmul(x, w_qkv)
+    q, k, v = np.split(proj, 3, axis=-1)
+    hd = q.shape[-1] // num_heads
+    shp = q.shape[:-1] + (num_heads, hd)
+    return q.reshape(shp), k.reshape(shp), v.reshape(shp)

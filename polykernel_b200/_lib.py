@@ -29,6 +29,8 @@ SIGNATURES = {
     "pkb200_matmul_peer_store_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
     "pkb200_reduce_slots_bias_residual": (c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P]),
     "pkb200_bias_residual_f32": (c_int, [_P, _P, _P, _P, c_int, c_int, _P]),
+    "pkb200_fused_residual_rmsnorm": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_float, _P]),
+    "pkb200_qkv_projection": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P]),
     "pkb200_matmul_int8": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_mlp_block_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "pkb200_mlp_block": (c_int, [_P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_float,

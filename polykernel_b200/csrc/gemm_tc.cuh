@@ -36,6 +36,7 @@ enum EpilogueKind : int {
   kEpiF32 = 4,        // C(fp32) = acc   (tensor-parallel partial sums)
   kEpiPeerStoreF32 = 6,  // owner(m).slot[src_rank][m % rows_per_rank, n] = acc (plain stores;
                          // the owner sums the slots afterwards)
+  kEpiQkvScatter = 7,    // bf16(acc) written to Q/K/V in [B, H, S, Dh] layout
 };
 
 constexpr int kMaxPeers = 8;
@@ -51,6 +52,9 @@ struct EpilogueArgs {
   float* peer[kMaxPeers];
   long long rows_per_rank;
   int src_rank;  // kEpiPeerStoreF32: this rank's slot index in every owner's buffer
+  // kEpiQkvScatter: row m = b*seq + s, column n = which*heads*head_dim + h*head_dim + e
+  __nv_bfloat16* qkv[3];
+  int seq, heads, head_dim;
 };
 
 
@@ -299,7 +303,15 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
               float a8[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) a8[j] = __uint_as_float(r[g * 8 + j]);
-              if constexpr (EPI == kEpiPeerStoreF32) {
+              if constexpr (EPI == kEpiQkvScatter) {
+                const int hd = ea.head_dim, width = ea.heads * hd;
+                const int which = n / width, rem = n - which * width;
+                const int hh = rem / hd, e = rem - hh * hd;
+                const long long b = m / ea.seq, sq = m - b * ea.seq;
+                __nv_bfloat16* dst =
+                    ea.qkv[which] + ((b * ea.heads + hh) * ea.seq + sq) * hd + e;
+                *reinterpret_cast<uint4*>(dst) = epilogue8<kEpiPlain>(a8, ea, m, n);
+              } else if constexpr (EPI == kEpiPeerStoreF32) {
                 const long long owner = m / ea.rows_per_rank;
                 float* dst = ea.peer[owner] +
                              (ea.src_rank * ea.rows_per_rank + (m - owner * ea.rows_per_rank)) * N + n;

@@ -149,6 +149,7 @@ const char* op_name(int epi) {
     case kEpiBiasResid: return "matmul_bias_residual";
     case kEpiColScale: return "matmul_int8";
     case kEpiF32: return "matmul_f32out";
+    case kEpiQkvScatter: return "qkv_projection";
     default: return "matmul_peer_store_f32";
   }
 }
@@ -647,6 +648,41 @@ int pkb200_reduce_slots_bias_residual(const float* slots, int world, int rows, i
   return cudaGetLastError();
 }
 
+int pkb200_fused_residual_rmsnorm(const void* x, const void* resid, const void* weight,
+                                  void* out, void* sum_out, int rows, int cols, float eps,
+                                  void* stream) {
+  if (rows < 0 || cols < 0) return cudaErrorInvalidValue;
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  if (!x || !resid || !out) return cudaErrorInvalidValue;
+  const int rows_per_block = 8;
+  const long long blocks = (static_cast<long long>(rows) + rows_per_block - 1) / rows_per_block;
+  residual_rmsnorm_rows_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0,
+                                 S(stream)>>>(cb(x), cb(resid), cb(weight), b(out), b(sum_out),
+                                              rows, cols, eps);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
+int pkb200_qkv_projection(const void* X, const void* W_qkv, void* Q, void* K_out, void* V, int B,
+                          int S_len, int H, int Dh, void* stream) {
+  if (B < 0 || S_len < 0 || H <= 0 || Dh <= 0) return cudaErrorInvalidValue;
+  if (B == 0 || S_len == 0) return cudaSuccess;
+  if (!X || !W_qkv || !Q || !K_out || !V) return cudaErrorInvalidValue;
+  const int M = B * S_len, Kd = H * Dh, N = 3 * Kd;
+  // the scatter epilogue writes 8-column groups, which must stay inside one head
+  if (Dh % 8 || Kd % 8 || !aligned16(Q) || !aligned16(K_out) || !aligned16(V) || !aligned16(X) ||
+      !aligned16(W_qkv))
+    return cudaErrorInvalidValue;
+  EpilogueArgs ea{};
+  ea.qkv[0] = b(Q);
+  ea.qkv[1] = b(K_out);
+  ea.qkv[2] = b(V);
+  ea.seq = S_len;
+  ea.heads = H;
+  ea.head_dim = Dh;
+  return run_gemm<kEpiQkvScatter>(cb(X), cb(W_qkv), Q, M, N, Kd, ea, S(stream));
+}
+
 int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
                              int M, int N, void* stream) {
   if (M < 0 || N < 0) return cudaErrorInvalidValue;
@@ -904,7 +940,7 @@ static void cfg_out(const tuning::Config& c, int* cfg7) {
 int pkb200_gemm_select(const char* op, int M, int N, int K, int* cfg7) {
   if (!op || !cfg7) return -1;
   int epi = -1;
-  for (int e = kEpiPlain; e <= kEpiPeerStoreF32; ++e)
+  for (int e = kEpiPlain; e <= kEpiQkvScatter; ++e)
     if (std::strcmp(op, op_name(e)) == 0) epi = e;
   if (std::strcmp(op, "fused_rmsnorm_matmul") == 0) epi = kEpiPlain;
   if (epi < 0) return -1;

@@ -91,6 +91,36 @@ __global__ void rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// ------------------------------------------------- residual add + RMSNorm --
+// t = bf16(x + resid) (golden.add), out = rmsnorm(t; weight, eps)
+// (golden.fused_residual_rmsnorm, golden.py:108-112). `sum_out` (nullable)
+// receives t, the new residual stream. One warp per row.
+__global__ void residual_rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                             const __nv_bfloat16* __restrict__ resid,
+                                             const __nv_bfloat16* __restrict__ weight,
+                                             __nv_bfloat16* __restrict__ out,
+                                             __nv_bfloat16* __restrict__ sum_out, long long rows,
+                                             int cols, float eps) {
+  const long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const long long base = r * cols;
+  float ss = 0.f;
+  for (int c = lane; c < cols; c += 32) {
+    const float t = bf16_round(__bfloat162float(x[base + c]) + __bfloat162float(resid[base + c]));
+    ss += t * t;
+    if (sum_out) sum_out[base + c] = __float2bfloat16_rn(t);
+  }
+  ss = warp_sum(ss);
+  const float rms = sqrtf(ss / static_cast<float>(cols) + eps);
+  for (int c = lane; c < cols; c += 32) {
+    const float t = bf16_round(__bfloat162float(x[base + c]) + __bfloat162float(resid[base + c]));
+    float a = __fdiv_rn(t, rms);
+    if (weight) a *= __bfloat162float(weight[c]);
+    out[base + c] = __float2bfloat16_rn(a);
+  }
+}
+
 // --------------------------------------------------------------------- GELU --
 // y = bf16(0.5 x (1 + erf(x/sqrt 2)))  (golden.py:63-66, gelu.cu:35-49).
 __global__ void gelu_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,

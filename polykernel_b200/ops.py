@@ -253,3 +253,36 @@ def attention_prefill_kv_append(q, k_new, v_new, k_cache, v_cache, s_cache, caus
         int(s_cache), Smax, D, float(scale), int(bool(causal)), _stream()),
         "attention_prefill_kv_append")
     return o
+
+
+def fused_residual_rmsnorm(x, residual, weight=None, eps=1e-5, return_sum=False):
+    """golden.fused_residual_rmsnorm: rmsnorm(bf16(x + residual)); optionally also
+    the rounded sum (the new residual stream)."""
+    _req(x, "x")
+    _req(residual, "residual")
+    if residual.shape != x.shape:
+        raise ValueError("x and residual must have the same shape")
+    if weight is not None:
+        _req(weight, "weight")
+    cols = x.shape[-1]
+    out = torch.empty_like(x)
+    ssum = torch.empty_like(x) if return_sum else None
+    check(lib().pkb200_fused_residual_rmsnorm(_ptr(x), _ptr(residual), _ptr(weight), _ptr(out),
+                                              _ptr(ssum), x.numel() // max(cols, 1), cols,
+                                              float(eps), _stream()), "fused_residual_rmsnorm")
+    return (out, ssum) if return_sum else out
+
+
+def qkv_projection(x, w_qkv, num_heads):
+    """golden.qkv_projection with Q, K, V returned in the attention layout
+    [B, H, S, Dh] (x is [B, S, H*Dh])."""
+    _req(x, "x", dims=3)
+    _req(w_qkv, "w_qkv", dims=2)
+    B, S, Dm = x.shape
+    if w_qkv.shape != (Dm, 3 * Dm) or Dm % num_heads:
+        raise ValueError("w_qkv must be [D, 3D] with D divisible by num_heads")
+    Dh = Dm // num_heads
+    q, k, v = (torch.empty(B, num_heads, S, Dh, dtype=BF16, device=x.device) for _ in range(3))
+    check(lib().pkb200_qkv_projection(_ptr(x), _ptr(w_qkv), _ptr(q), _ptr(k), _ptr(v), B, S,
+                                      num_heads, Dh, _stream()), "qkv_projection")
+    return q, k, v

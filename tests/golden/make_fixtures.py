@@ -137,6 +137,17 @@ def main():
     q8["w_float"], q8["wq_pc"], q8["scale_pc"] = bits(Wf), wq2, sc2
     q8["out_pc"] = bits(QG.matmul_int8(A, wq2, sc2))
     np.savez_compressed(os.path.join(HERE, "golden_int8.npz"), **q8)
+    # ------------------------------------------- next-row ops (residual+norm, QKV)
+    nx = {}
+    x = uni((6, 256)); res = uni((6, 256)); w = uni((256,))
+    nx["frr_x"], nx["frr_res"], nx["frr_w"] = bits(x), bits(res), bits(w)
+    nx["frr_out"] = bits(G.fused_residual_rmsnorm(x, res, w, 1e-6))
+    B_, S_, H_, Dh = 2, 64, 4, 64
+    x = uni((B_, S_, H_ * Dh)); wqkv = uni((H_ * Dh, 3 * H_ * Dh))
+    q, k, v = G.qkv_projection(x, wqkv, num_heads=H_)   # [B, S, H, Dh] each
+    nx["qkv_x"], nx["qkv_w"] = bits(x), bits(wqkv)
+    nx["qkv_q"], nx["qkv_k"], nx["qkv_v"] = bits(q), bits(k), bits(v)
+    np.savez_compressed(os.path.join(HERE, "golden_next.npz"), **nx)
     print("fixtures written to", HERE)
 
 

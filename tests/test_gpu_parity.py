@@ -198,3 +198,27 @@ def test_attention_mid_vs_oracle(pk):
     o = pk.ops.attention_prefill(*(t_from_bits(a) for a in (q, k, v)), causal=True)
     ref = O.attention_prefill(F(q), F(k), F(v), True)
     print("attn mid", check_attention(f32_from_t(o), ref))
+
+
+def test_fused_residual_rmsnorm_vs_golden(golden, pk):
+    g = golden("next")
+    x, res, w = (t_from_bits(g[k]) for k in ("frr_x", "frr_res", "frr_w"))
+    out, ssum = pk.ops.fused_residual_rmsnorm(x, res, w, eps=1e-6, return_sum=True)
+    check_gate(f32_from_t(out), F(g["frr_out"]), min_exact=0.99)
+    assert np.array_equal(bits_from_t(ssum), O.to_bits(O.add(F(g["frr_x"]), F(g["frr_res"]))))
+
+
+def test_qkv_projection_feeds_attention(golden, pk):
+    g = golden("next")
+    x, w = t_from_bits(g["qkv_x"]), t_from_bits(g["qkv_w"])
+    q, k, v = pk.ops.qkv_projection(x, w, num_heads=4)
+    Kd = g["qkv_w"].shape[0]
+    xf, wf = F(g["qkv_x"]), F(g["qkv_w"])
+    ref64 = np.split(O.matmul(xf, wf, acc=np.float64), 3, axis=-1)
+    for t, key, r64 in ((q, "qkv_q", ref64[0]), (k, "qkv_k", ref64[1]), (v, "qkv_v", ref64[2])):
+        gold = F(g[key]).transpose(0, 2, 1, 3)                 # golden [B,S,H,Dh] -> [B,H,S,Dh]
+        r64 = r64.reshape(gold.shape[0], gold.shape[2], gold.shape[1], gold.shape[3]).transpose(0, 2, 1, 3)
+        print(key, check_parity(f32_from_t(t), np.ascontiguousarray(gold), r64))
+    o = pk.ops.attention_prefill(q, k, v, causal=True)       # the layout attention consumes
+    check_attention(f32_from_t(o), O.attention_prefill(f32_from_t(q), f32_from_t(k), f32_from_t(v)))
+    assert Kd == 256

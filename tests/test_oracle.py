@@ -165,3 +165,12 @@ def test_parity_rule_accepts_reference_cpu_at_config1(golden, reflib):
                       ctypes.c_int64(512))
     m = check_parity(F(out), F(g["out"]))
     assert m["max_rel_err"] > Mx.MAX_REL_ERR_THRESHOLD  # the strict gate alone would reject it
+
+
+def test_next_row_fragments_bit_exact(golden):
+    g = golden("next")
+    out = O.fused_residual_rmsnorm(F(g["frr_x"]), F(g["frr_res"]), F(g["frr_w"]), 1e-6)
+    assert np.array_equal(O.to_bits(out), g["frr_out"])
+    q, k, v = O.qkv_projection(F(g["qkv_x"]), F(g["qkv_w"]), 4)
+    for a, key in ((q, "qkv_q"), (k, "qkv_k"), (v, "qkv_v")):
+        assert np.array_equal(O.to_bits(a), g[key])
