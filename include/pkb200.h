@@ -84,11 +84,12 @@ int pkb200_matmul_bias_residual(const void* A, const void* B, const void* bias,
                                 const void* resid, void* out, int M, int N, int K, void* stream);
 
 /* Tensor-parallel GEMM2 that moves its partial sums to their owners itself.
- * Row block r of this rank's fp32 partial A @ B is stored (plain 16-byte
- * stores, over NVLink for peers) into slot src_rank of peer_slots[r], an fp32
+ * Row block r of this rank's fp32 partial A @ B is stored (TMA bulk stores of
+ * 32x32 tiles, over NVLink for peers) into slot src_rank of peer_slots[r], an fp32
  * [world][M/world][N] buffer owned by rank r. After all ranks synchronise, each
  * owner runs pkb200_reduce_slots_bias_residual on its buffer.
- * world <= 8; M % world == 0; K, N multiples of 8. New; no reference counterpart. */
+ * world <= 8; M % world == 0 and (M / world) % 32 == 0; K, N multiples of 8.
+ * New; no reference counterpart. */
 int pkb200_matmul_peer_store_f32(const void* A, const void* B, float* const* peer_slots,
                                  int world, int src_rank, int M, int N, int K, void* stream);
 

@@ -41,6 +41,13 @@ enum EpilogueKind : int {
 
 constexpr int kMaxPeers = 8;
 
+// kEpiPeerStoreF32: one TMA map per owner rank over its [world*rows_per_rank, N]
+// fp32 slot buffer (box 32 columns x 32 rows, 128-byte swizzle). Passed as a
+// __grid_constant__ kernel parameter so the maps stay in parameter space.
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
+};
+
 struct EpilogueArgs {
   const __nv_bfloat16* bias;   // [N] or null
   const __nv_bfloat16* resid;  // [M, ld_resid] or null
@@ -139,6 +146,11 @@ constexpr int smem_bytes(int bn, int stages) {
   return stages * stage_bytes(bn) + 1024 /*align*/ + 256 /*barriers*/;
 }
 constexpr int tmem_cols(int bn) { return 2 * bn; }  // two accumulators
+// Peer-store epilogue staging: 8 epilogue warps x 2 buffers x (32 x 32 fp32).
+constexpr int kPeerStageBytes = 8 * 2 * 4096;
+constexpr int smem_bytes_peer(int bn, int stages) {
+  return stages * stage_bytes(bn) + 1024 /*barriers*/ + kPeerStageBytes + 1024 /*align*/;
+}
 constexpr int kMaxSmem = 232448;                    // 227 KB per CTA on sm_100
 }  // namespace gemm
 
@@ -156,7 +168,8 @@ template <int EPI, int BN, int STAGES>
 __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, void* __restrict__ C, long long ldc,
-                   int M, int N, int K, EpilogueArgs ea, int* err) {
+                   int M, int N, int K, EpilogueArgs ea, int* err,
+                   const __grid_constant__ PeerMaps peer_maps) {
   using gemm::BM;
   using gemm::BK;
   using gemm::EPI_THREADS;
@@ -165,7 +178,9 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
   constexpr int B_BLOCK_BYTES = BK * 64 * 2;  // one 64-wide N block
   constexpr int TMEM_COLS = gemm::tmem_cols(BN);
   static_assert(BN == 128 || BN == 256, "tile width");
-  static_assert(gemm::smem_bytes(BN, STAGES) <= gemm::kMaxSmem, "pipeline does not fit");
+  static_assert((EPI == kEpiPeerStoreF32 ? gemm::smem_bytes_peer(BN, STAGES)
+                                         : gemm::smem_bytes(BN, STAGES)) <= gemm::kMaxSmem,
+                "pipeline does not fit");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -279,6 +294,7 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     const int half = (warp - 2) >> 2;  // which 128-column half of the tile
     const int row = q * 32 + lane;
     int local = 0;
+    int peer_issue = 0;  // TMA stores issued by this warp (peer-store epilogue)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int mb, nb;
       tile_coords(t, tiles_m, tiles_n, mb, nb);
@@ -295,6 +311,29 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
         tmem_ld32(t_row + c * 32, r);
         tmem_ld_wait();
         const int n0 = nb * BN + c * 32;
+        if constexpr (EPI == kEpiPeerStoreF32) {
+          // Stage this warp's 32 rows x 32 columns (128-byte swizzled rows) and
+          // send them to the owner rank's slot buffer with one TMA store: full
+          // 128-byte lines over NVLink instead of per-thread 16-byte stores.
+          const long long m0 = static_cast<long long>(mb) * BM + q * 32;
+          const int owner = static_cast<int>(m0 / ea.rows_per_rank);
+          uint8_t* buf = smem + STAGES * STAGE_BYTES + 1024 + (warp - 2) * 8192 + (peer_issue & 1) * 4096;
+          if (lane == 0 && peer_issue >= 2) bulk_wait_group_read1();
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+                make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && m0 < M && n0 < N) {
+            const int y = static_cast<int>(ea.src_rank * ea.rows_per_rank + (m0 - owner * ea.rows_per_rank));
+            tma_store_2d(&peer_maps.m[owner], buf, n0, y);
+            bulk_commit_group();
+          }
+          ++peer_issue;
+          continue;
+        }
         if (m < M) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
@@ -311,12 +350,6 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
                 __nv_bfloat16* dst =
                     ea.qkv[which] + ((b * ea.heads + hh) * ea.seq + sq) * hd + e;
                 *reinterpret_cast<uint4*>(dst) = epilogue8<kEpiPlain>(a8, ea, m, n);
-              } else if constexpr (EPI == kEpiPeerStoreF32) {
-                const long long owner = m / ea.rows_per_rank;
-                float* dst = ea.peer[owner] +
-                             (ea.src_rank * ea.rows_per_rank + (m - owner * ea.rows_per_rank)) * N + n;
-                reinterpret_cast<float4*>(dst)[0] = make_float4(a8[0], a8[1], a8[2], a8[3]);
-                reinterpret_cast<float4*>(dst)[1] = make_float4(a8[4], a8[5], a8[6], a8[7]);
               } else if constexpr (EPI == kEpiF32) {
                 float* cp = static_cast<float*>(C) + m * ldc + n;
                 reinterpret_cast<float4*>(cp)[0] = make_float4(a8[0], a8[1], a8[2], a8[3]);
@@ -331,6 +364,9 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
+    }
+    if constexpr (EPI == kEpiPeerStoreF32) {
+      if (lane == 0) bulk_wait_group0();  // every store has landed before the kernel ends
     }
   }
 

@@ -194,8 +194,10 @@ tuning::Config select_config(int epi, int M, int N, int K, int* source = nullptr
 // -------------------------------------------------------------------- GEMM --
 template <int EPI, int BN, int STAGES>
 int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N,
-                        int K, const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di) {
-  constexpr int smem = gemm::smem_bytes(BN, STAGES);
+                        int K, const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di,
+                        const PeerMaps* peer = nullptr) {
+  constexpr int smem = EPI == kEpiPeerStoreF32 ? gemm::smem_bytes_peer(BN, STAGES)
+                                               : gemm::smem_bytes(BN, STAGES);
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -210,8 +212,9 @@ int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, i
   const int cap = g_gemm_max_ctas.load();
   if (cap > 0 && cap < ctas) ctas = cap;
   const int grid = tiles < ctas ? tiles : ctas;
+  static const PeerMaps kNoPeers{};
   gemm_tc_kernel<EPI, BN, STAGES><<<grid, gemm::NUM_THREADS, smem, s>>>(
-      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err, peer ? *peer : kNoPeers);
   g_counters[kCntGemmTc]++;
   return cudaGetLastError();
 }
@@ -234,16 +237,31 @@ int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
     if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, dims, str, box))
       return cudaErrorInvalidValue;
   }
-  const tuning::Config cfg = select_config(EPI, M, N, K);
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    g_last_cfg = cfg;
-  }
-  switch (variant_of(cfg)) {
-    case 1: return launch_gemm_variant<EPI, 256, 3>(ma, mb, C, M, N, K, ea, s, di);
-    case 2: return launch_gemm_variant<EPI, 128, 4>(ma, mb, C, M, N, K, ea, s, di);
-    case 3: return launch_gemm_variant<EPI, 128, 6>(ma, mb, C, M, N, K, ea, s, di);
-    default: return launch_gemm_variant<EPI, 256, 4>(ma, mb, C, M, N, K, ea, s, di);
+  if constexpr (EPI == kEpiPeerStoreF32) {
+    // fixed variant: 3 stages leave room for the store staging buffers
+    PeerMaps pm{};
+    const int world = static_cast<int>(M / ea.rows_per_rank);
+    for (int r = 0; r < world; ++r) {
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N),
+                                  static_cast<cuuint64_t>(world) * ea.rows_per_rank};
+      const cuuint64_t str[1] = {static_cast<cuuint64_t>(N) * 4};
+      const cuuint32_t box[2] = {32, 32};
+      if (!make_map(&pm.m[r], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ea.peer[r], dims, str, box))
+        return cudaErrorInvalidValue;
+    }
+    return launch_gemm_variant<EPI, 256, 3>(ma, mb, C, M, N, K, ea, s, di, &pm);
+  } else {
+    const tuning::Config cfg = select_config(EPI, M, N, K);
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      g_last_cfg = cfg;
+    }
+    switch (variant_of(cfg)) {
+      case 1: return launch_gemm_variant<EPI, 256, 3>(ma, mb, C, M, N, K, ea, s, di);
+      case 2: return launch_gemm_variant<EPI, 128, 4>(ma, mb, C, M, N, K, ea, s, di);
+      case 3: return launch_gemm_variant<EPI, 128, 6>(ma, mb, C, M, N, K, ea, s, di);
+      default: return launch_gemm_variant<EPI, 256, 4>(ma, mb, C, M, N, K, ea, s, di);
+    }
   }
 }
 
@@ -628,7 +646,9 @@ int pkb200_matmul_peer_store_f32(const void* A, const void* B, float* const* pee
   }
   ea.rows_per_rank = M / world;
   ea.src_rank = src_rank;
-  if (K <= 0 || K % 8 || N % 8 || !aligned16(A) || !aligned16(B)) return cudaErrorInvalidValue;
+  // 32-row store boxes must not straddle two owners; 16-byte aligned rows
+  if (ea.rows_per_rank % 32 || K <= 0 || K % 8 || N % 8 || !aligned16(A) || !aligned16(B))
+    return cudaErrorInvalidValue;
   return run_gemm<kEpiPeerStoreF32>(cb(A), cb(B), peer_slots[0], M, N, K, ea, S(stream));
 }
 
