@@ -390,6 +390,57 @@ def run_gpu_arm(args):
     a_flops = attn_flops(B, Hl, S, D)
     a_tflops = a_flops / (attn_ms * 1e-3) / 1e12
 
+    # The other BASELINE configs on one GPU (informational; not part of `value`).
+    others = None
+    if world == 1 and not args.no_others:
+        others = {}
+
+        def tflops_of(fn, flops, iters=10):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record(stream)
+            for _ in range(iters):
+                fn()
+            b_.record(stream)
+            torch.cuda.synchronize()
+            ms_ = a_.elapsed_time(b_) / iters
+            return {"ms": ms_, "tflops": flops / (ms_ * 1e-3) / 1e12}
+
+        gg = torch.Generator(device=dev).manual_seed(7)
+        M2, d2, f2 = 2048, 4096, 16384
+        x2 = torch.randn(M2, d2, device=dev, generator=gg).to(bf)
+        g2 = (1 + 0.1 * torch.randn(d2, device=dev, generator=gg)).to(bf)
+        w12 = (torch.randn(d2, f2, device=dev, generator=gg) / 64).to(bf)
+        b12 = (0.02 * torch.randn(f2, device=dev, generator=gg)).to(bf)
+        w22 = (torch.randn(f2, d2, device=dev, generator=gg) / 128).to(bf)
+        b22 = (0.02 * torch.randn(d2, device=dev, generator=gg)).to(bf)
+        ws2 = ops.mlp_workspace(M2, d2, f2, dev)
+        others["config2_mlp_block"] = tflops_of(
+            lambda: ops.mlp_block(x2, g2, w12, b12, w22, b22, eps, ws2), mlp_flops(M2, d2, f2))
+        del x2, w12, w22, ws2
+        M4, d4, f4 = 4096, 4096, 14336
+        x4 = torch.randn(M4, d4, device=dev, generator=gg).to(bf)
+        g4 = (1 + 0.1 * torch.randn(d4, device=dev, generator=gg)).to(bf)
+        q1 = torch.randint(-127, 128, (d4, f4), device=dev, generator=gg, dtype=torch.int8)
+        q2 = torch.randint(-127, 128, (f4, d4), device=dev, generator=gg, dtype=torch.int8)
+        s1 = (0.001 + 0.019 * torch.rand(f4, device=dev, generator=gg)).to(bf).float()
+        s2 = (0.001 + 0.019 * torch.rand(d4, device=dev, generator=gg)).to(bf).float()
+        b14 = (0.02 * torch.randn(f4, device=dev, generator=gg)).to(bf)
+        b24 = (0.02 * torch.randn(d4, device=dev, generator=gg)).to(bf)
+        ws4 = ops.mlp_workspace(M4, d4, f4, dev)
+        others["config4_int8_mlp_block"] = tflops_of(
+            lambda: ops.mlp_block_int8(x4, g4, q1, s1, b14, q2, s2, b24, eps, ws4),
+            mlp_flops(M4, d4, f4))
+        del x4, q1, q2, ws4
+        kcp = torch.randn(B, H, S_max, D, device=dev, generator=gg).to(bf)
+        vcp = torch.randn(B, H, S_max, D, device=dev, generator=gg).to(bf)
+        others["config3_attention_s_cache_2048"] = tflops_of(
+            lambda: ops.attention_prefill_kv_append(q, kn, vn, kcp, vcp, 2048, True, out=o),
+            attn_flops(B, H, S, D, 2048))
+        del kcp, vcp
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and os.path.exists(REF_LIB):
         import numpy as np
@@ -424,6 +475,7 @@ def run_gpu_arm(args):
             "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
+            "other_configs": others,
             "clocks": clocks,
             "device_error": err,
         }
@@ -446,6 +498,8 @@ def main():
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="row chunks of the host-streamed end-to-end MLP")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-others", action="store_true",
+                    help="skip the informational config-2/3/4 measurements")
     # DRAM bytes per config-5 GEMM1 launch: 1.71 GB measured by ncu at M=4096
     # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).
     ap.add_argument("--traffic", type=float, default=6.83e9,
