@@ -113,11 +113,11 @@ def matmul_int8(a, wq, scale, acc=F32):
     return bf16(np.matmul(bf16(a).astype(acc), wdeq.astype(acc)).astype(F32))
 
 
-def mlp_block_int8(x, gamma, w1q, s1, b1, w2q, s2, b2, eps=1e-6):
+def mlp_block_int8(x, gamma, w1q, s1, b1, w2q, s2, b2, eps=1e-6, acc=F32):
     """int8 weight-only MLP chain: each matmul is quant_golden.matmul_int8, the
     rest as mlp_block."""
-    h = gelu(bias(matmul_int8(rmsnorm(x, gamma, eps), w1q, s1), b1))
-    return add(bias(matmul_int8(h, w2q, s2), b2), x)
+    h = gelu(bias(matmul_int8(rmsnorm(x, gamma, eps), w1q, s1, acc), b1))
+    return add(bias(matmul_int8(h, w2q, s2, acc), b2), x)
 
 
 # ----------------------------------------------------------------- attention --
