@@ -433,7 +433,11 @@ def run_gpu_arm(args):
         others["config4_int8_mlp_block"] = tflops_of(
             lambda: ops.mlp_block_int8(x4, g4, q1, s1, b14, q2, s2, b24, eps, ws4),
             mlp_flops(M4, d4, f4))
-        del x4, q1, q2, ws4
+        # fp8 (e4m3) weight-only GEMM at config 4's GEMM1 shape, weights resident as fp8
+        w8 = ops.quantize_fp8((torch.randn(d4, f4, device=dev, generator=gg) / 64).to(bf), "e4m3")
+        others["config4_shape_fp8_e4m3_gemm1"] = tflops_of(
+            lambda: ops.matmul_fp8(x4, w8), 2.0 * M4 * d4 * f4)
+        del x4, q1, q2, ws4, w8
         kcp = torch.randn(B, H, S_max, D, device=dev, generator=gg).to(bf)
         vcp = torch.randn(B, H, S_max, D, device=dev, generator=gg).to(bf)
         others["config3_attention_s_cache_2048"] = tflops_of(

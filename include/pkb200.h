@@ -127,6 +127,23 @@ int pkb200_qkv_projection(const void* X, const void* W_qkv, void* Q, void* K, vo
 int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void* C, int M,
                        int N, int K, void* stream);
 
+/* fp8 weight path (fmt 0 = e4m3fn, 1 = e5m2). The reference only simulates
+ * fp8 weights (tests/golden/quant_golden.py:116-125, matmul_fp8_sim;
+ * kernels/cpu/matmul_quant.cpp:130-160 and its `fp8sim` mode :207-236);
+ * these entry points keep the weights in HBM as one byte per element.
+ * pkb200_quantize_fp8: W bf16 [n] -> fp8 codes [n], round-to-nearest-even,
+ *   saturating like the reference's fp8_round (matmul_quant.cpp:130-150).
+ * pkb200_dequantize_fp8: fp8 codes [n] -> bf16 [n] (exact).
+ * pkb200_matmul_fp8: C = bf16(A @ fp8(W)); A bf16 [M,K], Wf8 codes [K,N].
+ * pkb200_matmul_fp8_sim: the reference's simulated path with bf16 W [K,N]
+ *   (round onto the fp8 grid, then matmul); same result as quantize + matmul_fp8. */
+int pkb200_quantize_fp8(const void* W, uint8_t* Wf8, long long n, int fmt, void* stream);
+int pkb200_dequantize_fp8(const uint8_t* Wf8, void* W, long long n, int fmt, void* stream);
+int pkb200_matmul_fp8(const void* A, const uint8_t* Wf8, void* C, int M, int N, int K, int fmt,
+                      void* stream);
+int pkb200_matmul_fp8_sim(const void* A, const void* W, void* C, int M, int N, int K, int fmt,
+                          void* stream);
+
 /* Bytes of device workspace pkb200_mlp_block / pkb200_mlp_block_int8 need. */
 size_t pkb200_mlp_block_workspace_size(int M, int d, int ffn);
 

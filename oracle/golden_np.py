@@ -120,6 +120,80 @@ def mlp_block_int8(x, gamma, w1q, s1, b1, w2q, s2, b2, eps=1e-6, acc=F32):
     return add(bias(matmul_int8(h, w2q, s2, acc), b2), x)
 
 
+# ------------------------------------------------------- fp8 weight path --
+# (e4m3fn: 3 mantissa bits, bias 7, max finite 448, no inf; e5m2: 2 mantissa
+# bits, bias 15, max finite 57344, IEEE inf/NaN.)
+FP8_FORMATS = {"e4m3": (3, 7, 448.0, False), "e5m2": (2, 15, 57344.0, True)}
+
+
+def fp8_round(x, fmt):
+    """Round onto the fp8 grid, returned as float32 (the reference's CPU
+    fp8_round, kernels/cpu/matmul_quant.cpp:130-150): NaN stays NaN, +-inf
+    saturates to +-max-finite for e4m3 and stays inf for e5m2, finite
+    magnitudes above max-finite saturate, the rest round to nearest-even at
+    the value's own exponent (fixed smallest ulp below the normal range), and
+    a result rounded past max-finite is clamped. Signed zeros are kept."""
+    mbits, bias_, fmax, has_inf = FP8_FORMATS[fmt]
+    x = np.asarray(x, dtype=F32)
+    mag = np.abs(x).astype(np.float64)
+    finite = np.isfinite(mag)
+    m = np.where(finite, np.minimum(mag, fmax), 0.0)
+    emin = 1 - bias_
+    _, e = np.frexp(np.where(m > 0, m, 1.0))
+    ex = np.maximum(e - 1, emin)
+    ulp = np.ldexp(1.0, ex - mbits)
+    r = np.minimum(np.rint(m / ulp) * ulp, fmax)
+    inf_val = np.inf if has_inf else fmax
+    r = np.where(np.isinf(mag), inf_val, r)
+    r = np.where(np.isnan(x), np.nan, np.copysign(r, x))
+    return r.astype(F32)
+
+
+def fp8_bits(x, fmt):
+    """fp8 encoding (uint8) of values already on the fp8 grid (fp8_round's
+    output): sign, biased exponent, mantissa; NaN -> 0x7F|sign."""
+    mbits, bias_, _, _ = FP8_FORMATS[fmt]
+    x = np.asarray(x, dtype=F32)
+    sign = np.signbit(x).astype(np.uint8) << 7
+    mag = np.abs(x).astype(np.float64)
+    emin = 1 - bias_
+    out = np.zeros(x.shape, np.uint8)
+    sub = mag < 2.0 ** emin
+    out = np.where(sub, np.rint(mag / 2.0 ** (emin - mbits)), out)
+    _, e = np.frexp(np.where(mag > 0, mag, 1.0))
+    ex = e - 1
+    frac = np.rint((mag / np.ldexp(1.0, ex) - 1.0) * (1 << mbits))
+    normal = ~sub & np.isfinite(mag)
+    out = np.where(normal, ((ex + bias_) << mbits) + frac, out)
+    out = np.where(np.isinf(mag), (0x1F << 2) if fmt == "e5m2" else 0x7E, out)
+    out = np.where(np.isnan(x), 0x7F, out)
+    return out.astype(np.uint8) | sign
+
+
+def fp8_decode(bits, fmt):
+    """fp8 bits -> float32 (exact; every fp8 value is a bf16 value)."""
+    mbits, bias_, _, has_inf = FP8_FORMATS[fmt]
+    b = np.asarray(bits, dtype=np.uint8).astype(np.int64)
+    s = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> mbits) & ((1 << (7 - mbits)) - 1)
+    m = b & ((1 << mbits) - 1)
+    emax_field = (1 << (7 - mbits)) - 1
+    v = np.where(e == 0, m * 2.0 ** (1 - bias_ - mbits),
+                 (1.0 + m / (1 << mbits)) * np.ldexp(1.0, e - bias_))
+    if has_inf:
+        v = np.where(e == emax_field, np.where(m == 0, np.inf, np.nan), v)
+    else:
+        v = np.where((e == emax_field) & (m == (1 << mbits) - 1), np.nan, v)
+    return (s * v).astype(F32)
+
+
+def matmul_fp8_sim(a, w, fmt, acc=F32):
+    """quant_golden.matmul_fp8_sim (quant_golden.py:116-125): weight-only fp8,
+    C = bf16(fp32(bf16(A)) @ fp8(bf16(W)))."""
+    w8 = fp8_round(bf16(w), fmt)
+    return bf16(np.matmul(bf16(a).astype(acc), w8.astype(acc)).astype(F32))
+
+
 # ----------------------------------------------------------------- attention --
 def attention_prefill(q, k, v, causal=True, scale=None):
     """Prefill SDPA (kernels/cpu/attention.cpp:95-163; golden.py:139-172):

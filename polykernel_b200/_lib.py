@@ -32,6 +32,10 @@ SIGNATURES = {
     "pkb200_fused_residual_rmsnorm": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_float, _P]),
     "pkb200_qkv_projection": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P]),
     "pkb200_matmul_int8": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    "pkb200_quantize_fp8": (c_int, [_P, _P, c_longlong, c_int, _P]),
+    "pkb200_dequantize_fp8": (c_int, [_P, _P, c_longlong, c_int, _P]),
+    "pkb200_matmul_fp8": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P]),
+    "pkb200_matmul_fp8_sim": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P]),
     "pkb200_mlp_block_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "pkb200_mlp_block": (c_int, [_P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_float,
                                  _P, c_size_t, _P]),

@@ -3,7 +3,7 @@
 // read bf16 .npy inputs, copy them to the device, call the library's entry
 // point, copy the result back and write a bf16 .npy. Same op names, argument
 // order, defaults (--epsilon 1e-5) and exit codes (0 ok, 1 runtime error,
-// 2 usage), plus the ops this library adds (mlp_block, matmul_int8,
+// 2 usage), plus the ops this library adds (mlp_block, matmul_int8, fp8sim,
 // attention_prefill, kv_cache_update, attention_append).
 //
 // bf16 arrays use NumPy's '<V2' void descr (raw 16-bit brain-float values), as
@@ -291,6 +291,28 @@ int run_matmul_int8(int argc, char** argv) {
   return st;
 }
 
+// fp8sim <e4m3|e5m2> A W OUT: the simulated fp8 weight path with the argument
+// order of the reference's CPU driver (kernels/cpu/matmul_quant.cpp:168, `fp8sim`).
+int run_fp8sim(int argc, char** argv) {
+  if (argc != 6) return usage("fp8sim <e4m3|e5m2> A W OUT   (A bf16 [M,K], W bf16 [K,N])");
+  const std::string fmt = argv[2];
+  if (fmt != "e4m3" && fmt != "e5m2") return usage("fp8sim: format must be e4m3 or e5m2");
+  Npy a = read_npy(argv[3], "<V2"), w = read_npy(argv[4], "<V2");
+  const int64_t K = a.shape.back(), M = a.size() / K, N = w.shape[1];
+  if (w.shape[0] != K) {
+    std::fprintf(stderr, "fp8sim: contraction mismatch\n");
+    return 1;
+  }
+  std::fprintf(stderr, "[pkb200-cuda_run] path=fp8_sim fmt=%s M=%lld N=%lld K=%lld\n",
+               fmt.c_str(), (long long)M, (long long)N, (long long)K);
+  Dev da(a), dw(w), dout(static_cast<size_t>(M * N) * 2);
+  int st = finish(pkb200_matmul_fp8_sim(da.p, dw.p, dout.p, (int)M, (int)N, (int)K,
+                                        fmt == "e4m3" ? 0 : 1, nullptr),
+                  "fp8sim");
+  if (!st) download(dout, with_last(a.shape, N), argv[5]);
+  return st;
+}
+
 int run_mlp_block(int argc, char** argv) {
   const char* u = "mlp_block X GAMMA W1 B1 W2 B2 OUT [--epsilon E]";
   if (argc < 9) return usage(u);
@@ -405,6 +427,7 @@ int main(int argc, char** argv) {
     if (op == "fused_rmsnorm_matmul") return run_fused_rmsnorm_matmul(argc, argv);
     if (op == "fused_matmul_bias_gelu") return run_fused_matmul_bias_gelu(argc, argv);
     if (op == "matmul_int8") return run_matmul_int8(argc, argv);
+    if (op == "fp8sim") return run_fp8sim(argc, argv);
     if (op == "mlp_block") return run_mlp_block(argc, argv);
     if (op == "attention_prefill") return run_attention_prefill(argc, argv);
     if (op == "kv_cache_update") return run_kv_cache_update(argc, argv);

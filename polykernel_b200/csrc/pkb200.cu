@@ -15,6 +15,7 @@
 #include <utility>
 
 #include "attention_tc.cuh"
+#include "fp8.cuh"
 #include "simt_kernels.cuh"
 #include "tuning.h"
 #include "../../include/pkb200.h"
@@ -354,6 +355,32 @@ int run_int8_expand(const int8_t* q, bf16* out, long long n, cudaStream_t s, Dev
   return cudaGetLastError();
 }
 
+
+// fp8 passes over n elements. kind: 0 = bf16 -> fp8 codes, 1 = fp8 codes ->
+// bf16, 2 = bf16 -> bf16 on the fp8 grid.
+int run_fp8_pass(int kind, int fmt, const void* in, void* out, long long n, cudaStream_t s,
+                 DeviceInfo* di) {
+  if (fmt != kFp8E4M3 && fmt != kFp8E5M2) return cudaErrorInvalidValue;
+  if (n < 0) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  if (!in || !out) return cudaErrorInvalidValue;
+  const bool vec = aligned16(in) && aligned16(out);
+  const int grid = grid_for(vec ? n / 8 + 1 : n, 256, di);
+  const bf16* ib = static_cast<const bf16*>(in);
+  const uint8_t* i8 = static_cast<const uint8_t*>(in);
+  if (kind == 0) {
+    if (fmt == kFp8E4M3) bf16_to_fp8_kernel<kFp8E4M3><<<grid, 256, 0, s>>>(ib, static_cast<uint8_t*>(out), n, vec);
+    else bf16_to_fp8_kernel<kFp8E5M2><<<grid, 256, 0, s>>>(ib, static_cast<uint8_t*>(out), n, vec);
+  } else if (kind == 1) {
+    if (fmt == kFp8E4M3) fp8_to_bf16_kernel<kFp8E4M3><<<grid, 256, 0, s>>>(i8, static_cast<bf16*>(out), n, vec);
+    else fp8_to_bf16_kernel<kFp8E5M2><<<grid, 256, 0, s>>>(i8, static_cast<bf16*>(out), n, vec);
+  } else {
+    if (fmt == kFp8E4M3) bf16_round_fp8_grid_kernel<kFp8E4M3><<<grid, 256, 0, s>>>(ib, static_cast<bf16*>(out), n, vec);
+    else bf16_round_fp8_grid_kernel<kFp8E5M2><<<grid, 256, 0, s>>>(ib, static_cast<bf16*>(out), n, vec);
+  }
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
 
 // --------------------------------------------------------------- attention --
 template <int D>
@@ -748,6 +775,50 @@ int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void
   e = run_int8_expand(Wq, b(ws), static_cast<long long>(K) * N, S(stream), di);
   if (e) return e;
   return run_gemm<kEpiColScale>(cb(A), cb(ws), C, M, N, K, ea, S(stream));
+}
+
+int pkb200_quantize_fp8(const void* W, uint8_t* Wf8, long long n, int fmt, void* stream) {
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  return run_fp8_pass(0, fmt, W, Wf8, n, S(stream), di);
+}
+
+int pkb200_dequantize_fp8(const uint8_t* Wf8, void* W, long long n, int fmt, void* stream) {
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  return run_fp8_pass(1, fmt, Wf8, W, n, S(stream), di);
+}
+
+// Shared body of the two fp8 GEMMs: expand (kind 1) or round (kind 2) the
+// weights into bf16 workspace, then the bf16 GEMM.
+static int matmul_fp8_impl(int kind, const void* A, const void* W, void* C, int M, int N, int K,
+                           int fmt, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
+  if (fmt != kFp8E4M3 && fmt != kFp8E5M2) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (!A || !W || !C) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  void* ws = nullptr;
+  const long long kn = static_cast<long long>(K) * N;
+  e = library_workspace(align_up(static_cast<size_t>(kn > 128 ? kn : 128) * 2), S(stream), &ws);
+  if (e) return e;
+  e = run_fp8_pass(kind, fmt, W, ws, kn, S(stream), di);
+  if (e) return e;
+  return run_gemm<kEpiPlain>(cb(A), cb(ws), C, M, N, K, EpilogueArgs{}, S(stream));
+}
+
+int pkb200_matmul_fp8(const void* A, const uint8_t* Wf8, void* C, int M, int N, int K, int fmt,
+                      void* stream) {
+  return matmul_fp8_impl(1, A, Wf8, C, M, N, K, fmt, stream);
+}
+
+int pkb200_matmul_fp8_sim(const void* A, const void* W, void* C, int M, int N, int K, int fmt,
+                          void* stream) {
+  return matmul_fp8_impl(2, A, W, C, M, N, K, fmt, stream);
 }
 
 size_t pkb200_mlp_block_workspace_size(int M, int d, int ffn) {

@@ -157,6 +157,74 @@ def matmul_int8(a, wq, scale):
     return c
 
 
+FP8_FORMATS = {"e4m3": (0, torch.float8_e4m3fn), "e5m2": (1, torch.float8_e5m2)}
+
+
+def _fp8_fmt(fmt):
+    if fmt not in FP8_FORMATS:
+        raise ValueError(f"unknown fp8 format {fmt!r} (expected 'e4m3' or 'e5m2')")
+    return FP8_FORMATS[fmt]
+
+
+def quantize_fp8(w, fmt="e4m3"):
+    """bf16 -> fp8 weights (torch.float8_e4m3fn / float8_e5m2 tensor), rounded
+    to nearest-even and saturating like the reference's CPU fp8_round
+    (kernels/cpu/matmul_quant.cpp:130-150)."""
+    code, dt = _fp8_fmt(fmt)
+    _req(w, "w")
+    out = torch.empty(w.shape, dtype=dt, device=w.device)
+    check(lib().pkb200_quantize_fp8(_ptr(w), _ptr(out), w.numel(), code, _stream()),
+          "quantize_fp8")
+    return out
+
+
+def dequantize_fp8(wf8):
+    """fp8 weights -> bf16 (exact)."""
+    fmt = {torch.float8_e4m3fn: "e4m3", torch.float8_e5m2: "e5m2"}.get(wf8.dtype)
+    if fmt is None:
+        raise TypeError(f"wf8: expected a float8_e4m3fn/float8_e5m2 tensor, got {wf8.dtype}")
+    _req(wf8, "wf8", dtype=wf8.dtype)
+    out = torch.empty(wf8.shape, dtype=BF16, device=wf8.device)
+    check(lib().pkb200_dequantize_fp8(_ptr(wf8), _ptr(out), wf8.numel(), FP8_FORMATS[fmt][0],
+                                      _stream()), "dequantize_fp8")
+    return out
+
+
+def matmul_fp8(a, wf8):
+    """C = bf16(A @ fp8(W)) with the weights resident as fp8 [K, N]
+    (quant_golden.matmul_fp8_sim semantics, quant_golden.py:116-125)."""
+    fmt = {torch.float8_e4m3fn: "e4m3", torch.float8_e5m2: "e5m2"}.get(wf8.dtype)
+    if fmt is None:
+        raise TypeError(f"wf8: expected a float8_e4m3fn/float8_e5m2 tensor, got {wf8.dtype}")
+    _req(a, "a")
+    _req(wf8, "wf8", dtype=wf8.dtype, dims=2)
+    K, N = wf8.shape
+    if a.shape[-1] != K:
+        raise ValueError("shape mismatch")
+    M = a.numel() // max(K, 1)
+    c = torch.empty(*a.shape[:-1], N, dtype=BF16, device=a.device)
+    check(lib().pkb200_matmul_fp8(_ptr(a), _ptr(wf8), _ptr(c), M, N, K, FP8_FORMATS[fmt][0],
+                                  _stream()), "matmul_fp8")
+    return c
+
+
+def matmul_fp8_sim(a, w, fmt="e4m3"):
+    """The reference's simulated fp8 path (quant_golden.matmul_fp8_sim; the CPU
+    `fp8sim` mode, matmul_quant.cpp:207-236): bf16 W rounded onto the fp8 grid,
+    then matmul."""
+    code, _ = _fp8_fmt(fmt)
+    _req(a, "a")
+    _req(w, "w", dims=2)
+    K, N = w.shape
+    if a.shape[-1] != K:
+        raise ValueError("shape mismatch")
+    M = a.numel() // max(K, 1)
+    c = torch.empty(*a.shape[:-1], N, dtype=BF16, device=a.device)
+    check(lib().pkb200_matmul_fp8_sim(_ptr(a), _ptr(w), _ptr(c), M, N, K, code, _stream()),
+          "matmul_fp8_sim")
+    return c
+
+
 def mlp_workspace(M, d, ffn, device=None):
     n = int(lib().pkb200_mlp_block_workspace_size(M, d, ffn))
     return torch.empty(max(n, 1), dtype=torch.uint8, device=device or "cuda")

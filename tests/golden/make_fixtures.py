@@ -7,7 +7,7 @@ The fixtures (golden_*.npz, bf16 stored as raw uint16 bits) are committed; the
 GPU tests and the oracle self-tests read only those files, never the reference.
 
 Cases mirror the reference's own tests (test_golden_self.py, test_cuda_run.py,
-test_attention.py, test_quant.py, tests/e2e mini-MLP) plus the BASELINE config-1
+test_attention.py, test_quant.py incl. its fp8 simulation, tests/e2e mini-MLP) plus the BASELINE config-1
 fragment and shapes that exercise the tensor-core tiles (multi-tile, partial
 tiles, two-source KV).
 """
@@ -148,6 +148,27 @@ def main():
     nx["qkv_x"], nx["qkv_w"] = bits(x), bits(wqkv)
     nx["qkv_q"], nx["qkv_k"], nx["qkv_v"] = bits(q), bits(k), bits(v)
     np.savez_compressed(os.path.join(HERE, "golden_next.npz"), **nx)
+    # -------------------------------------------- fp8 weight path (simulated)
+    f8 = {}
+    for fmt, dt in (("e4m3", ml_dtypes.float8_e4m3fn), ("e5m2", ml_dtypes.float8_e5m2)):
+        for (m, k, n) in ((128, 128, 128), (192, 160, 224)):  # test_quant.py:205-206
+            a, w = uni((m, k)), uni((k, n))
+            key = f"{fmt}_{m}x{k}x{n}"
+            f8[f"{key}_a"], f8[f"{key}_w"] = bits(a), bits(w)
+            f8[f"{key}_out"] = bits(QG.matmul_fp8_sim(a, w, fmt))
+        # rounding edge values within the format's range: ties, subnormals,
+        # values next to max-finite, signed zeros (the golden's ml_dtypes cast)
+        lim = 448.0 if fmt == "e4m3" else 57344.0
+        mags = np.concatenate([
+            rng.uniform(0, 1, 512), rng.uniform(0, lim, 512),
+            np.exp2(rng.uniform(-20, -5, 512)), [0.0, lim, lim * 0.97, 2.0 ** -9, 2.0 ** -16,
+                                                 1.0625, 1.1875, 0.015625 * 1.0625]])
+        sgn = np.where(rng.uniform(size=mags.shape) < 0.5, -1.0, 1.0)
+        e = (sgn * mags).astype(np.float32).astype(BF)
+        e = e[np.abs(e.astype(np.float32)) <= lim]
+        f8[f"{fmt}_edge_in"] = bits(e)
+        f8[f"{fmt}_edge_code"] = e.astype(dt).view(np.uint8)
+    np.savez_compressed(os.path.join(HERE, "golden_fp8.npz"), **f8)
     print("fixtures written to", HERE)
 
 

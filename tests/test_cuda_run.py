@@ -103,3 +103,22 @@ def test_mlp_and_attention_through_harness(golden, cuda, tmp_path):
     assert _run("attention_prefill", tmp_path / "q.npy", tmp_path / "k.npy", tmp_path / "v.npy",
                 tmp_path / "o.npy").returncode == 0
     check_attention(F(_load(tmp_path / "o.npy")), F(a["d128_o"]))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_fp8sim_through_harness(golden, cuda, tmp_path, fmt):
+    """`fp8sim <fmt> A W OUT`, the argument order of the reference's CPU driver
+    (kernels/cpu/matmul_quant.cpp `fp8sim`), against its golden fixture."""
+    g = golden("fp8")
+    case = f"{fmt}_192x160x224"
+    _save(tmp_path / "a.npy", g[f"{case}_a"])
+    _save(tmp_path / "w.npy", g[f"{case}_w"])
+    r = _run("fp8sim", fmt, tmp_path / "a.npy", tmp_path / "w.npy", tmp_path / "c.npy")
+    assert r.returncode == 0 and "path=fp8_sim" in r.stderr, r.stderr
+    check_gate(F(_load(tmp_path / "c.npy")), F(g[f"{case}_out"]), rel_ceiling=5e-2,
+               min_exact=0.99, quant=True)
+
+
+def test_fp8sim_usage():
+    assert _run("fp8sim", "e3m4", "a.npy", "w.npy", "c.npy").returncode == 2

@@ -174,3 +174,62 @@ def test_next_row_fragments_bit_exact(golden):
     q, k, v = O.qkv_projection(F(g["qkv_x"]), F(g["qkv_w"]), 4)
     for a, key in ((q, "qkv_q"), (k, "qkv_k"), (v, "qkv_v")):
         assert np.array_equal(O.to_bits(a), g[key])
+
+
+# ----------------------------------------------------------- fp8 weight path
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_fp8_rounding_matches_golden_cast(golden, fmt):
+    """fp8_round + fp8_bits reproduce the golden's ml_dtypes cast code for code
+    on ties, subnormals, values next to max-finite and signed zeros."""
+    g = golden("fp8")
+    x = F(g[f"{fmt}_edge_in"])
+    r = O.fp8_round(x, fmt)
+    assert np.array_equal(O.fp8_bits(r, fmt), g[f"{fmt}_edge_code"])
+    assert np.array_equal(O.fp8_decode(g[f"{fmt}_edge_code"], fmt), r)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_fp8_code_table_round_trip(fmt):
+    codes = np.arange(256, dtype=np.uint8)
+    v = O.fp8_decode(codes, fmt)
+    finite = np.isfinite(v)
+    assert np.array_equal(O.fp8_bits(O.fp8_round(v[finite], fmt), fmt), codes[finite])
+    assert np.array_equal(O.bf16(v[finite]), v[finite])  # every fp8 value is a bf16 value
+
+
+@pytest.mark.parametrize("case", ["e4m3_128x128x128", "e4m3_192x160x224",
+                                  "e5m2_128x128x128", "e5m2_192x160x224"])
+def test_fp8_sim_matmul_bit_exact(golden, case):
+    g = golden("fp8")
+    fmt = case.split("_")[0]
+    out = O.matmul_fp8_sim(F(g[f"{case}_a"]), F(g[f"{case}_w"]), fmt)
+    assert np.array_equal(O.to_bits(out), g[f"{case}_out"])
+
+
+def fp8_edge_weights(fmt):
+    """Values that exercise saturation and rounding at the top of the range,
+    where the golden's ml_dtypes cast and the reference's CPU code differ."""
+    lim = 448.0 if fmt == "e4m3" else 57344.0
+    v = np.array([lim, lim * 1.03, lim * 1.07, lim * 4, 1e30, 3e38, 1.0, 1.0625, 1.1875,
+                  2.0 ** -9, 2.0 ** -10, 3 * 2.0 ** -11, 2.0 ** -16, 2.0 ** -17, 3 * 2.0 ** -18,
+                  0.0], np.float32)
+    return O.bf16(np.concatenate([v, -v]))
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_reference_cpu_fp8_rounding_matches_oracle(tmp_path, fmt):
+    """The reference's own CPU driver (oracle/_ref/matmul_quant fp8sim) with an
+    identity A returns fp8(W) itself: pins fp8_round's saturation and rounding."""
+    import subprocess
+    exe = os.path.join(os.path.dirname(REF_LIB), "matmul_quant")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref not built (make -C oracle)")
+    w = fp8_edge_weights(fmt).reshape(4, 8)
+    eye = np.eye(4, dtype=np.float32)
+    np.save(tmp_path / "a.npy", O.to_bits(eye).view("V2"))
+    np.save(tmp_path / "w.npy", O.to_bits(w).view("V2"))
+    subprocess.run([exe, "fp8sim", fmt, str(tmp_path / "a.npy"), str(tmp_path / "w.npy"),
+                    str(tmp_path / "c.npy")], check=True, capture_output=True)
+    c = F(np.load(tmp_path / "c.npy").view(np.uint16))
+    # compared as values: the driver's fp32 sum turns fp8(-0) into +0
+    assert np.array_equal(c, O.fp8_round(w, fmt))
