@@ -133,8 +133,11 @@ def fp8_round(x, fmt):
     magnitudes above max-finite saturate, the rest round to nearest-even at
     the value's own exponent (fixed smallest ulp below the normal range), and
     a result rounded past max-finite is clamped. Signed zeros are kept."""
-    mbits, bias_, fmax, has_inf = FP8_FORMATS[fmt]
-    x = np.asarray(x, dtype=F32)
+    with np.errstate(invalid="ignore"):
+        return _fp8_round(np.asarray(x, dtype=F32), *FP8_FORMATS[fmt])
+
+
+def _fp8_round(x, mbits, bias_, fmax, has_inf):
     mag = np.abs(x).astype(np.float64)
     finite = np.isfinite(mag)
     m = np.where(finite, np.minimum(mag, fmax), 0.0)
