@@ -29,6 +29,11 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# The copy-engine exchange keeps ~2 streams per peer busy; give each its own
+# hardware queue so a stream waiting on a peer's flag cannot hold up another.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+# stdout carries exactly one JSON line; NCCL's own start-up banner stays off it
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 MLP_CFG = dict(M=16384, d=8192, ffn=28672, eps=1e-6)
 ATTN_CFG = dict(B=4, H=32, S=2048, D=128, S_max=4096)
@@ -217,7 +222,12 @@ def run_gpu_arm(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        # NCCL's internal streams at high priority: when a GEMM chunk ends, the
+        # collective's CTAs are placed before the next chunk's (the GEMM's
+        # dynamic tile schedule lets it run on the SMs that remain)
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", device_id=dev, pg_options=opts)
     pk.lib()
 
     M, d, ffn, eps = MLP_CFG["M"], MLP_CFG["d"], MLP_CFG["ffn"], MLP_CFG["eps"]
@@ -250,13 +260,14 @@ def run_gpu_arm(args):
         mlp = lambda xx, out: ops.mlp_block(xx, gamma, w1, b1, w2, b2, eps, ws, out)  # noqa
         launches_per_step = 3 + 1
     else:
-        tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks,
-                                fused_reduce=args.tp_mode == "fused")
+        reduce = {"fused": "peer_store", "nccl": "nccl", "ce": "copy_engine"}[args.tp_mode]
+        tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks, reduce=reduce,
+                                per_peer_streams=not args.tp_one_stream)
 
         def mlp(xx, out):
-            out.copy_(tpm(xx))
-            return out
-        launches_per_step = (2 + 2 + 1) if args.tp_mode == "fused" else (2 + 2 * args.tp_chunks + 1)
+            return tpm(xx, out=out)
+        launches_per_step = {"fused": 2 + 2 + 1, "nccl": 2 + 2 * args.tp_chunks + 1,
+                             "ce": 2 + 2 * args.tp_chunks}[args.tp_mode]
 
     stream = torch.cuda.current_stream()
     # events around the dominant kernel (GEMM1 with the bias+GELU epilogue) are
@@ -466,6 +477,7 @@ def run_gpu_arm(args):
                        "mlp": {"M": M, "d": d, "ffn": ffn}, "attention":
                        {"B": B, "H": H, "S": S, "D": D, "S_cache": 0, "cache_rows": S_max},
                        "parallelism": f"tp{world} (MLP) / heads{world} (attention)",
+                       "tp_exchange": args.tp_mode if world > 1 else None,
                        "l2": "inputs larger than L2 (no flush needed)"},
             "parts": {"mlp_tflops": mlp_flops(M, d, ffn) / ((ms - attn_ms) * 1e-3) / 1e12,
                       "attention_ms": attn_ms, "attention_tflops_whole_job": a_tflops * world,
@@ -496,9 +508,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="pkb200", choices=["pkb200", "reference"])
     ap.add_argument("--tp-chunks", type=int, default=4)
-    ap.add_argument("--tp-mode", default="nccl", choices=["fused", "nccl"],
-                    help="nccl: chunked GEMM2 + NCCL reduce-scatter/all-gather (default); "
-                         "fused: GEMM2 epilogue stores partials into the owners' buffers over NVLink")
+    ap.add_argument("--tp-one-stream", action="store_true",
+                    help="copy-engine exchange: one push and one pull stream for all peers")
+    ap.add_argument("--tp-mode", default="ce", choices=["ce", "fused", "nccl"],
+                    help="ce: chunked GEMM2, copy-engine push of the fp32 partials to their owners "
+                         "and pull of the reduced rows (default); nccl: chunked GEMM2 + NCCL "
+                         "reduce-scatter/all-gather; fused: GEMM2 epilogue stores partials into "
+                         "the owners' buffers over NVLink")
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="row chunks of the host-streamed end-to-end MLP")
     ap.add_argument("--no-cpu", action="store_true")

@@ -105,6 +105,53 @@ int pkb200_reduce_slots_bias_residual(const float* slots, int world, int rows, i
 int pkb200_bias_residual_f32(const float* Y, const void* bias, const void* resid, void* out,
                              int M, int N, void* stream);
 
+/* Tile schedule of the persistent tcgen05 GEMM: 1 (default) = each CTA takes
+ * its next tile from a per-launch atomic counter, so CTAs that start late
+ * (SMs held by a concurrent kernel such as a collective) take fewer tiles;
+ * 0 = fixed stride over the tiles by CTA index. Results are identical. */
+int pkb200_set_gemm_schedule(int dynamic);
+
+/* Stream memory operations for the copy-engine tensor-parallel exchange (new;
+ * the reference has no multi-GPU path): `stream` waits until the 32-bit word
+ * at `addr` (device memory of this GPU) is >= `value`, cyclically compared;
+ * or writes `value` to `addr` in stream order. Both run on the GPU's front end
+ * and hold no SM. */
+int pkb200_stream_wait_value32(void* stream, const void* addr, unsigned int value);
+int pkb200_stream_write_value32(void* stream, void* addr, unsigned int value);
+
+/* Copy-engine tensor-parallel MLP exchange (new; the reference has no
+ * multi-GPU path). W1 is column-split and W2 row-split over `world` ranks;
+ * each rank calls pkb200_tp_ce_mlp_step after its GEMM1 (h = its [M, ffn/world]
+ * shard of gelu(rmsnorm(x) @ W1 + b1)). The step runs GEMM2 in `chunks` row
+ * chunks on `stream`; after each chunk the copy engines push every fp32
+ * partial row block to the rank that owns it (slots), the owner sums the
+ * slots in rank order with the b2 + residual epilogue, and the copy engines
+ * gather the bf16 rows into `out` [M, d] on every rank.
+ * Buffers (peer pointers in this process's address space, e.g. from
+ * pkb200_ipc_alloc / pkb200_ipc_open): slots[p] fp32 [chunks][world][M/chunks/world][d],
+ * rows[p] bf16 [chunks][M/chunks/world][d], flags[p] uint32 [2][chunks][world]
+ * zeroed before first use, on every rank; y32 fp32 [M, d] and epoch_src
+ * uint32 [2*8+2] local to this rank. `epoch` increases by 1 per step from 1.
+ * pkb200_tp_ce_wait waits on the host for the last step, at most
+ * `timeout_ms`; when a peer has not delivered by then it releases this rank's
+ * waits, marks the plan failed and returns cudaErrorTimeout (the context
+ * stays usable; create a new plan after the failure). */
+/* Peer mappings without multicast: device memory this library allocates
+ * (zeroed) with its 64-byte CUDA IPC handle, opened by the peer processes;
+ * used for the copy-engine exchange's slots, rows and flags. */
+int pkb200_ipc_alloc(size_t bytes, void** ptr, void* handle64);
+int pkb200_ipc_open(const void* handle64, void** ptr);
+int pkb200_ipc_close(void* ptr);
+int pkb200_free(void* ptr);
+int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_peer_streams,
+                        float* y32, float* const* slots, void* const* rows,
+                        unsigned int* const* flags, unsigned int* epoch_src, void** plan_out);
+int pkb200_tp_ce_destroy(void* plan);
+int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_shard,
+                          const void* b2, const void* x, void* out, unsigned int epoch,
+                          void* stream);
+int pkb200_tp_ce_wait(void* plan, int timeout_ms);
+
 /* out = rmsnorm(bf16(x + resid); weight, eps) over the last axis
  * (golden.fused_residual_rmsnorm, tests/golden/golden.py:108-112): the residual
  * add + next-layer norm that follows the MLP. sum_out (nullable) receives the

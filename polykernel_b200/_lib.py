@@ -32,6 +32,18 @@ SIGNATURES = {
     "pkb200_fused_residual_rmsnorm": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_float, _P]),
     "pkb200_qkv_projection": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P]),
     "pkb200_matmul_int8": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    "pkb200_set_gemm_schedule": (c_int, [c_int]),
+    "pkb200_stream_wait_value32": (c_int, [_P, _P, ctypes.c_uint]),
+    "pkb200_stream_write_value32": (c_int, [_P, _P, ctypes.c_uint]),
+    "pkb200_ipc_alloc": (c_int, [c_size_t, _P, _P]),
+    "pkb200_ipc_open": (c_int, [_P, _P]),
+    "pkb200_ipc_close": (c_int, [_P]),
+    "pkb200_free": (c_int, [_P]),
+    "pkb200_tp_ce_create": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P,
+                                    _P]),
+    "pkb200_tp_ce_destroy": (c_int, [_P]),
+    "pkb200_tp_ce_mlp_step": (c_int, [_P, _P, _P, c_int, _P, _P, _P, ctypes.c_uint, _P]),
+    "pkb200_tp_ce_wait": (c_int, [_P, c_int]),
     "pkb200_quantize_fp8": (c_int, [_P, _P, c_longlong, c_int, _P]),
     "pkb200_dequantize_fp8": (c_int, [_P, _P, c_longlong, c_int, _P]),
     "pkb200_matmul_fp8": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P]),

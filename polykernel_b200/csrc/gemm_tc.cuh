@@ -137,13 +137,14 @@ constexpr int BK = 64;
 constexpr int NUM_THREADS = 320;            // 2 control warps + 8 epilogue warps
 constexpr int EPI_THREADS = 256;
 constexpr int GROUP_M = 16;                 // rasterisation group (L2 reuse)
+constexpr int SCHED_DEPTH = 8;              // tile ids in flight producer -> consumers
 // Tunable per launch (the tuning cache's block_n / shared_memory_stages):
 // tile width BN in {128, 256} and pipeline depth STAGES.
 constexpr int a_bytes() { return BM * BK * 2; }
 constexpr int b_bytes(int bn) { return BK * bn * 2; }
 constexpr int stage_bytes(int bn) { return a_bytes() + b_bytes(bn); }
 constexpr int smem_bytes(int bn, int stages) {
-  return stages * stage_bytes(bn) + 1024 /*align*/ + 256 /*barriers*/;
+  return stages * stage_bytes(bn) + 1024 /*align*/ + 512 /*barriers, tile ring*/;
 }
 constexpr int tmem_cols(int bn) { return 2 * bn; }  // two accumulators
 // Peer-store epilogue staging: 8 epilogue warps x 2 buffers x (32 x 32 fp32).
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, void* __restrict__ C, long long ldc,
                    int M, int N, int K, EpilogueArgs ea, int* err,
-                   const __grid_constant__ PeerMaps peer_maps) {
+                   const __grid_constant__ PeerMaps peer_maps, int* tile_counter) {
   using gemm::BM;
   using gemm::BK;
   using gemm::EPI_THREADS;
@@ -188,7 +189,11 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  // tile-id ring from the producer to the MMA issuer and the epilogue warps
+  uint64_t* sched_full = tempty_bar + 2;
+  uint64_t* sched_empty = sched_full + gemm::SCHED_DEPTH;
+  volatile int* sched_tile = reinterpret_cast<volatile int*>(sched_empty + gemm::SCHED_DEPTH);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(sched_tile) + gemm::SCHED_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = warp_id();
@@ -206,6 +211,10 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], EPI_THREADS);
+    }
+    for (int i = 0; i < gemm::SCHED_DEPTH; ++i) {
+      mbar_init(&sched_full[i], 1);
+      mbar_init(&sched_empty[i], 1 + EPI_THREADS / 32);  // MMA issuer + one lane per epilogue warp
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -229,9 +238,26 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int slot = 0;
+      uint32_t sphase = 0;
+      // First tile by CTA index, the rest from the launch's counter when one
+      // is given (CTAs that start late, e.g. behind a collective holding some
+      // SMs, then take fewer tiles), else by stride.
+      int t = blockIdx.x;
+      while (ok) {
+        if (!mbar_wait(&sched_empty[slot], sphase ^ 1, err, abort_flag, kErrTimeoutProducer)) break;
+        sched_tile[slot] = t < num_tiles ? t : -1;
+        mbar_arrive(&sched_full[slot]);
+        if (++slot == gemm::SCHED_DEPTH) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (t >= num_tiles) break;
+        const int next = tile_counter ? static_cast<int>(gridDim.x) + atomicAdd(tile_counter, 1)
+                                      : t + static_cast<int>(gridDim.x);
         int mb, nb;
         tile_coords(t, tiles_m, tiles_n, mb, nb);
+        t = next;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag, kErrTimeoutProducer)) {
             ok = false;
@@ -259,7 +285,17 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      int slot = 0;
+      uint32_t sphase = 0;
+      for (;; ++local) {
+        if (!mbar_wait(&sched_full[slot], sphase, err, abort_flag, kErrTimeoutMma)) break;
+        const int t = sched_tile[slot];
+        mbar_arrive(&sched_empty[slot]);
+        if (++slot == gemm::SCHED_DEPTH) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (t < 0 || !ok) break;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err, abort_flag, kErrTimeoutMma)) break;
@@ -295,7 +331,18 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     const int row = q * 32 + lane;
     int local = 0;
     int peer_issue = 0;  // TMA stores issued by this warp (peer-store epilogue)
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    int slot = 0;
+    uint32_t sphase = 0;
+    for (;; ++local) {
+      if (!mbar_wait(&sched_full[slot], sphase, err, abort_flag, kErrTimeoutEpilogue)) break;
+      const int t = sched_tile[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sched_empty[slot]);
+      if (++slot == gemm::SCHED_DEPTH) {
+        slot = 0;
+        sphase ^= 1;
+      }
+      if (t < 0) break;
       int mb, nb;
       tile_coords(t, tiles_m, tiles_n, mb, nb);
       const int acc = local & 1;

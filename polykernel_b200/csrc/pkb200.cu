@@ -6,11 +6,14 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <chrono>
+#include <thread>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
 #include <sstream>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <utility>
 
@@ -78,6 +81,19 @@ EncodeTiledFn encode_fn() {
     return reinterpret_cast<EncodeTiledFn>(p);
   }();
   return fn;
+}
+
+// Stream memory operations (executed by the GPU's front end, no SM involved):
+// the flag waits and flag writes of the copy-engine tensor-parallel exchange.
+using StreamValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+StreamValue32Fn stream_value_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion(name, &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<StreamValue32Fn>(p);
 }
 
 // Rank-r tiled map with 128-byte swizzle. dims[0] is the contiguous axis.
@@ -193,6 +209,27 @@ tuning::Config select_config(int epi, int M, int N, int K, int* source = nullptr
 }
 
 // -------------------------------------------------------------------- GEMM --
+// Tile counters of the dynamic GEMM schedule: one per launch, taken round
+// robin and zeroed in stream order before the launch (launches in flight at
+// the same time on different streams get different counters).
+constexpr int kNumTileCounters = 256;
+__device__ int g_tile_counters[kNumTileCounters];
+std::atomic<int> g_gemm_dynamic{1};
+std::atomic<unsigned> g_tile_counter_next{0};
+
+int next_tile_counter(int dev, int** out) {
+  static int* base[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!base[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_tile_counters);
+    if (e != cudaSuccess) return e;
+    base[dev] = static_cast<int*>(p);
+  }
+  *out = base[dev] + (g_tile_counter_next.fetch_add(1) % kNumTileCounters);
+  return cudaSuccess;
+}
+
 template <int EPI, int BN, int STAGES>
 int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N,
                         int K, const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di,
@@ -214,8 +251,15 @@ int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, i
   if (cap > 0 && cap < ctas) ctas = cap;
   const int grid = tiles < ctas ? tiles : ctas;
   static const PeerMaps kNoPeers{};
+  int* counter = nullptr;
+  if (g_gemm_dynamic.load() && tiles > grid) {
+    int e = next_tile_counter(dev, &counter);
+    if (e) return e;
+    if ((e = cudaMemsetAsync(counter, 0, sizeof(int), s))) return e;
+  }
   gemm_tc_kernel<EPI, BN, STAGES><<<grid, gemm::NUM_THREADS, smem, s>>>(
-      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err, peer ? *peer : kNoPeers);
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err, peer ? *peer : kNoPeers,
+      counter);
   g_counters[kCntGemmTc]++;
   return cudaGetLastError();
 }
@@ -611,6 +655,146 @@ int noalloc_scratch(bf16** out) {
   return cudaSuccess;
 }
 
+// ------------------------------------------- copy-engine tensor parallel --
+// One tensor-parallel MLP step's exchange, planned once per shape. GEMM2 runs
+// in `chunks` row chunks on the caller's stream; after chunk i each rank's
+// copy engines push the fp32 partial row block that rank p owns straight into
+// p's slot buffer (slots[i][src]) and then a 4-byte epoch flag behind it in
+// the same copy stream. The owner's reduce stream waits for the flags with
+// stream memory operations (no SM is held while waiting), sums the slots in
+// rank order with the bias + residual epilogue, and raises its own "rows
+// ready" flag on every peer; the peers' pull streams then copy those bf16
+// rows into their outputs. The SMs run only the GEMMs and the short reduce
+// kernels; the NVLink traffic is driven by the copy engines and overlaps the
+// next chunk's GEMM.
+//
+// Buffer reuse needs no barrier: a rank pushes into p's slots[i] in step e+1
+// only after it finished step e, which includes pulling p's rows of step e,
+// which p published only after reducing slots[i] of step e. Likewise p's rows
+// buffer is rewritten in step e+1 only after p saw every rank's step e+1 push
+// flags, i.e. after every rank finished step e.
+constexpr int kMaxTpChunks = 64;
+
+struct TpCePlan {
+  int world = 0, rank = 0, chunks = 0, rows = 0, per = 0, d = 0, M = 0, device = 0;
+  float* y32 = nullptr;                   // local GEMM2 partials [M, d]
+  float* slots[kMaxPeers] = {};           // rank p's slots [chunks][world][per][d] fp32
+  bf16* mine[kMaxPeers] = {};             // rank p's reduced rows [chunks][per][d] bf16
+  unsigned* flags[kMaxPeers] = {};        // rank p's flags [2][chunks][world]
+  unsigned* epoch_src = nullptr;          // local words [2 * kMaxPeers + 2]
+  // one push and one pull stream per peer, or one of each for all peers
+  int nstreams = 0;
+  cudaStream_t push[kMaxPeers] = {}, pull[kMaxPeers] = {}, red = nullptr, release = nullptr;
+  cudaEvent_t ev_gemm[kMaxTpChunks] = {}, ev_end[2 * kMaxPeers + 1] = {}, ev_step = nullptr,
+              ev_done = nullptr;
+  unsigned last_epoch = 0;
+  bool aborted = false;
+  cudaStream_t push_for(int p) const { return push[nstreams == 1 ? 0 : p]; }
+  cudaStream_t pull_for(int p) const { return pull[nstreams == 1 ? 0 : p]; }
+  unsigned* flag_rs(int owner, int chunk, int src) const {
+    return flags[owner] + (0 * chunks + chunk) * world + src;
+  }
+  unsigned* flag_ag(int owner, int chunk, int src) const {
+    return flags[owner] + (1 * chunks + chunk) * world + src;
+  }
+};
+
+int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const bf16* bias,
+               const bf16* resid, bf16* out, unsigned epoch, cudaStream_t main) {
+  const int W = pl->world, me = pl->rank, C = pl->chunks, rows = pl->rows, per = pl->per;
+  const int d = pl->d;
+  const size_t blk_f32 = static_cast<size_t>(per) * d * 4, blk_bf16 = static_cast<size_t>(per) * d * 2;
+  auto ck = [](cudaError_t e) { return static_cast<int>(e); };
+  static StreamValue32Fn wait_fn = stream_value_fn("cuStreamWaitValue32");
+  static StreamValue32Fn write_fn = stream_value_fn("cuStreamWriteValue32");
+  if (!wait_fn || !write_fn) return cudaErrorNotSupported;
+  auto wait_v = [&](cudaStream_t s, const unsigned* a) {
+    return wait_fn(s, reinterpret_cast<CUdeviceptr>(a), epoch, CU_STREAM_WAIT_VALUE_GEQ) == CUDA_SUCCESS
+               ? 0 : static_cast<int>(cudaErrorUnknown);
+  };
+  auto write_v = [&](cudaStream_t s, unsigned* a) {
+    return write_fn(s, reinterpret_cast<CUdeviceptr>(a), epoch, CU_STREAM_WRITE_VALUE_DEFAULT) == CUDA_SUCCESS
+               ? 0 : static_cast<int>(cudaErrorUnknown);
+  };
+  int e;
+  // every stream starts after the caller's earlier work (h, x, out are ready)
+  if ((e = ck(cudaEventRecord(pl->ev_step, main)))) return e;
+  // peers are visited from me+1 upwards (destinations staggered across ranks);
+  // `first` marks the first use of a stream when all peers share one
+  for (int k = 1; k < W; ++k) {
+    const int p = (me + k) % W;
+    if (pl->nstreams == 1 && k != 1) continue;
+    if ((e = ck(cudaStreamWaitEvent(pl->push_for(p), pl->ev_step, 0)))) return e;
+    if ((e = ck(cudaStreamWaitEvent(pl->pull_for(p), pl->ev_step, 0)))) return e;
+  }
+  for (int k = 1; k < W; ++k)
+    if ((e = write_v(pl->push_for((me + k) % W), pl->epoch_src + (me + k) % W))) return e;
+  if ((e = ck(cudaStreamWaitEvent(pl->red, pl->ev_step, 0)))) return e;
+  if ((e = write_v(pl->red, pl->epoch_src + kMaxPeers))) return e;
+  for (int i = 0; i < C; ++i) {
+    const size_t row0 = static_cast<size_t>(i) * rows;
+    float* yc = pl->y32 + row0 * d;
+    if ((e = run_gemm<kEpiF32>(h + row0 * ffn_shard, w2, yc, rows, d, ffn_shard, EpilogueArgs{}, main)))
+      return e;
+    if ((e = ck(cudaEventRecord(pl->ev_gemm[i], main)))) return e;
+    // push: my partial of p's row block -> p's slots[i][me], then the flag
+    for (int k = 1; k < W; ++k) {
+      const int p = (me + k) % W;
+      cudaStream_t s = pl->push_for(p);
+      if ((pl->nstreams > 1 || k == 1) && (e = ck(cudaStreamWaitEvent(s, pl->ev_gemm[i], 0))))
+        return e;
+      float* dst = pl->slots[p] + (static_cast<size_t>(i) * W + me) * per * d;
+      if ((e = ck(cudaMemcpyAsync(dst, yc + static_cast<size_t>(p) * per * d, blk_f32, cudaMemcpyDefault, s))))
+        return e;
+      if ((e = ck(cudaMemcpyAsync(pl->flag_rs(p, i, me), pl->epoch_src + p, 4, cudaMemcpyDefault, s))))
+        return e;
+    }
+    // reduce: own block in, wait for the peers' blocks, sum + epilogue, publish
+    cudaStream_t r = pl->red;
+    if ((e = ck(cudaStreamWaitEvent(r, pl->ev_gemm[i], 0)))) return e;
+    float* my_slots = pl->slots[me] + static_cast<size_t>(i) * W * per * d;
+    if ((e = ck(cudaMemcpyAsync(my_slots + static_cast<size_t>(me) * per * d,
+                                yc + static_cast<size_t>(me) * per * d, blk_f32, cudaMemcpyDefault, r))))
+      return e;
+    for (int k = 1; k < W; ++k)
+      if ((e = wait_v(r, pl->flag_rs(me, i, (me + k) % W)))) return e;
+    bf16* rows_out = pl->mine[me] + static_cast<size_t>(i) * per * d;
+    const size_t own0 = (row0 + static_cast<size_t>(me) * per) * d;
+    if ((e = pkb200_reduce_slots_bias_residual(my_slots, W, per, d, bias, resid + own0, rows_out, r)))
+      return e;
+    if ((e = ck(cudaMemcpyAsync(out + own0, rows_out, blk_bf16, cudaMemcpyDefault, r)))) return e;
+    for (int k = 1; k < W; ++k) {
+      const int p = (me + k) % W;
+      if ((e = ck(cudaMemcpyAsync(pl->flag_ag(p, i, me), pl->epoch_src + kMaxPeers, 4, cudaMemcpyDefault, r))))
+        return e;
+    }
+    // pull: p's reduced rows of chunk i -> my output
+    for (int k = 1; k < W; ++k) {
+      const int p = (me + W - k) % W;  // pull first from the peer that pushed to me first
+      cudaStream_t s = pl->pull_for(p);
+      if ((e = wait_v(s, pl->flag_ag(me, i, p)))) return e;
+      const size_t dst0 = (row0 + static_cast<size_t>(p) * per) * d;
+      if ((e = ck(cudaMemcpyAsync(out + dst0, pl->mine[p] + static_cast<size_t>(i) * per * d, blk_bf16,
+                                  cudaMemcpyDefault, s))))
+        return e;
+    }
+  }
+  // the caller's stream continues once every copy and the last reduce are done
+  int k = 0;
+  for (int k = 1; k < W; ++k) {
+    const int p = (me + k) % W;
+    if (pl->nstreams == 1 && k != 1) continue;
+    for (cudaStream_t s : {pl->push_for(p), pl->pull_for(p)}) {
+      if ((e = ck(cudaEventRecord(pl->ev_end[k], s)))) return e;
+      if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k++], 0)))) return e;
+    }
+  }
+  if ((e = ck(cudaEventRecord(pl->ev_end[k], pl->red)))) return e;
+  if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k], 0)))) return e;
+  pl->last_epoch = epoch;
+  return ck(cudaEventRecord(pl->ev_done, main));
+}
+
 }  // namespace
 
 // =================================================================== C ABI ==
@@ -693,6 +877,152 @@ int pkb200_reduce_slots_bias_residual(const float* slots, int world, int rows, i
       slots, world, static_cast<long long>(rows) * N, N, cb(bias), cb(resid), b(out));
   g_counters[kCntOther]++;
   return cudaGetLastError();
+}
+
+int pkb200_set_gemm_schedule(int dynamic) {
+  g_gemm_dynamic.store(dynamic ? 1 : 0);
+  return cudaSuccess;
+}
+
+int pkb200_stream_wait_value32(void* stream, const void* addr, unsigned int value) {
+  static StreamValue32Fn fn = stream_value_fn("cuStreamWaitValue32");
+  if (!fn) return cudaErrorNotSupported;
+  if (!addr || (reinterpret_cast<uintptr_t>(addr) & 3u)) return cudaErrorInvalidValue;
+  const CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(addr), value,
+                        CU_STREAM_WAIT_VALUE_GEQ);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+}
+
+int pkb200_stream_write_value32(void* stream, void* addr, unsigned int value) {
+  static StreamValue32Fn fn = stream_value_fn("cuStreamWriteValue32");
+  if (!fn) return cudaErrorNotSupported;
+  if (!addr || (reinterpret_cast<uintptr_t>(addr) & 3u)) return cudaErrorInvalidValue;
+  const CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(addr), value,
+                        CU_STREAM_WRITE_VALUE_DEFAULT);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+}
+
+int pkb200_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return cudaErrorInvalidValue;
+  *ptr = nullptr;
+  int e = cudaMalloc(ptr, bytes);
+  if (e) return e;
+  if ((e = cudaMemset(*ptr, 0, bytes)) ||
+      (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr)) ||
+      (e = cudaDeviceSynchronize())) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return e;
+  }
+  return cudaSuccess;
+}
+
+int pkb200_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+int pkb200_ipc_close(void* ptr) { return ptr ? cudaIpcCloseMemHandle(ptr) : cudaSuccess; }
+
+int pkb200_free(void* ptr) { return ptr ? cudaFree(ptr) : cudaSuccess; }
+
+int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_peer_streams,
+                        float* y32, float* const* slots, void* const* rows, unsigned* const* flags,
+                        unsigned* epoch_src, void** plan_out) {
+  if (!plan_out) return cudaErrorInvalidValue;
+  *plan_out = nullptr;
+  if (world < 2 || world > kMaxPeers || rank < 0 || rank >= world || chunks < 1 ||
+      chunks > kMaxTpChunks || M <= 0 || d <= 0 || M % chunks || (M / chunks) % world || d % 4)
+    return cudaErrorInvalidValue;
+  if (!y32 || !slots || !rows || !flags || !epoch_src) return cudaErrorInvalidValue;
+  auto pl = std::make_unique<TpCePlan>();
+  pl->world = world; pl->rank = rank; pl->chunks = chunks; pl->M = M; pl->d = d;
+  pl->rows = M / chunks; pl->per = pl->rows / world;
+  pl->y32 = y32; pl->epoch_src = epoch_src;
+  for (int p = 0; p < world; ++p) {
+    if (!slots[p] || !rows[p] || !flags[p] || !aligned16(slots[p]) || !aligned16(rows[p]))
+      return cudaErrorInvalidValue;
+    pl->slots[p] = slots[p];
+    pl->mine[p] = static_cast<bf16*>(rows[p]);
+    pl->flags[p] = flags[p];
+  }
+  int e = cudaGetDevice(&pl->device);
+  if (e) return e;
+  int lo = 0, hi = 0;
+  cudaDeviceGetStreamPriorityRange(&lo, &hi);
+  pl->nstreams = per_peer_streams ? world : 1;
+  for (int i = 0; i < pl->nstreams; ++i) {
+    if ((e = cudaStreamCreateWithFlags(&pl->push[i], cudaStreamNonBlocking))) return e;
+    if ((e = cudaStreamCreateWithFlags(&pl->pull[i], cudaStreamNonBlocking))) return e;
+  }
+  // the reduce kernels go ahead of the next GEMM chunk's CTAs when SMs free up
+  if ((e = cudaStreamCreateWithPriority(&pl->red, cudaStreamNonBlocking, hi))) return e;
+  if ((e = cudaStreamCreateWithFlags(&pl->release, cudaStreamNonBlocking))) return e;
+  for (int i = 0; i < chunks; ++i)
+    if ((e = cudaEventCreateWithFlags(&pl->ev_gemm[i], cudaEventDisableTiming))) return e;
+  for (int i = 0; i < 2 * kMaxPeers + 1; ++i)
+    if ((e = cudaEventCreateWithFlags(&pl->ev_end[i], cudaEventDisableTiming))) return e;
+  if ((e = cudaEventCreateWithFlags(&pl->ev_step, cudaEventDisableTiming))) return e;
+  if ((e = cudaEventCreateWithFlags(&pl->ev_done, cudaEventDisableTiming))) return e;
+  *plan_out = pl.release();
+  return cudaSuccess;
+}
+
+int pkb200_tp_ce_destroy(void* plan) {
+  auto* pl = static_cast<TpCePlan*>(plan);
+  if (!pl) return cudaSuccess;
+  for (int i = 0; i < pl->nstreams; ++i) {
+    if (pl->push[i]) cudaStreamDestroy(pl->push[i]);
+    if (pl->pull[i]) cudaStreamDestroy(pl->pull[i]);
+  }
+  if (pl->red) cudaStreamDestroy(pl->red);
+  if (pl->release) cudaStreamDestroy(pl->release);
+  for (auto ev : pl->ev_gemm) if (ev) cudaEventDestroy(ev);
+  for (auto ev : pl->ev_end) if (ev) cudaEventDestroy(ev);
+  if (pl->ev_step) cudaEventDestroy(pl->ev_step);
+  if (pl->ev_done) cudaEventDestroy(pl->ev_done);
+  delete pl;
+  return cudaSuccess;
+}
+
+int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_shard,
+                          const void* b2, const void* x, void* out, unsigned int epoch,
+                          void* stream) {
+  auto* pl = static_cast<TpCePlan*>(plan);
+  if (!pl || !h || !w2 || !b2 || !x || !out || ffn_shard <= 0) return cudaErrorInvalidValue;
+  if (pl->aborted) return cudaErrorLaunchFailure;
+  if (epoch == 0 || static_cast<int>(epoch - pl->last_epoch) <= 0) return cudaErrorInvalidValue;
+  return tp_ce_step(pl, cb(h), cb(w2), ffn_shard, cb(b2), cb(x), b(out), epoch, S(stream));
+}
+
+int pkb200_tp_ce_wait(void* plan, int timeout_ms) {
+  auto* pl = static_cast<TpCePlan*>(plan);
+  if (!pl) return cudaErrorInvalidValue;
+  const auto t0 = std::chrono::steady_clock::now();
+  auto elapsed_ms = [&] {
+    return std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0)
+        .count();
+  };
+  while (true) {
+    const cudaError_t q = cudaEventQuery(pl->ev_done);
+    if (q == cudaSuccess) return pl->aborted ? cudaErrorTimeout : cudaSuccess;
+    if (q != cudaErrorNotReady) return q;
+    if (!pl->aborted && elapsed_ms() > timeout_ms) {
+      // A peer did not deliver in time. Release every local flag so the
+      // blocked stream waits complete (the step's output is then invalid),
+      // and poison the plan; the error is reported to the caller.
+      static StreamValue32Fn write_fn = stream_value_fn("cuStreamWriteValue32");
+      const unsigned v = pl->last_epoch + (1u << 30);
+      for (int i = 0; i < 2 * pl->chunks * pl->world; ++i)
+        write_fn(pl->release, reinterpret_cast<CUdeviceptr>(pl->flags[pl->rank] + i), v,
+                 CU_STREAM_WRITE_VALUE_DEFAULT);
+      pl->aborted = true;
+    }
+    if (pl->aborted && elapsed_ms() > 4LL * timeout_ms + 1000) return cudaErrorTimeout;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
 }
 
 int pkb200_fused_residual_rmsnorm(const void* x, const void* resid, const void* weight,

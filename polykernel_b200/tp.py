@@ -11,7 +11,16 @@ only the fp32 summation order changes.
 The reference has no multi-GPU path; this is new. With `chunks` > 1
 the rows of GEMM2 are processed in chunks whose reduction (reduce-scatter of
 the fp32 partials, epilogue on this rank's rows, all-gather of the bf16
-result) runs on a side stream and overlaps GEMM2 of the next chunk.
+result) overlaps GEMM2 of the next chunk. Three exchanges implement it:
+
+* "copy_engine" (pkb200_tp_ce_*): the copy engines push each partial row block
+  into its owner's slot buffer (torch symmetric memory) with an epoch flag
+  behind it; the owner waits on the flags with stream memory operations, sums
+  the slots and publishes its rows, which the peers' copy engines pull. No SM
+  is spent on data movement, so the persistent GEMM keeps every SM.
+* "nccl": NCCL reduce-scatter + all-gather on a side stream.
+* "peer_store": the GEMM2 epilogue itself stores the partial tiles into the
+  owners' slot buffers over NVLink (pkb200_matmul_peer_store_f32).
 """
 from __future__ import annotations
 
@@ -40,8 +49,11 @@ class TensorParallelMLP:
     implementation to check the sharding and reduction logic under gloo).
     """
 
+    REDUCERS = ("nccl", "peer_store", "copy_engine")
+
     def __init__(self, gamma, w1_shard, b1_shard, w2_shard, b2, eps=1e-6, group=None, kern=None,
-                 chunks=1, fused_reduce=False, comm_sms=0):
+                 chunks=1, fused_reduce=False, comm_sms=0, reduce=None, per_peer_streams=True,
+                 timeout_ms=60000):
         if kern is None:
             from . import ops as kern
         self.kern = kern
@@ -51,7 +63,14 @@ class TensorParallelMLP:
         self.chunks = max(1, int(chunks))
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self._comm = None
-        self.fused_reduce = fused_reduce
+        self.reduce = reduce or ("peer_store" if fused_reduce else "nccl")
+        if self.reduce not in self.REDUCERS:
+            raise ValueError(f"reduce must be one of {self.REDUCERS}, got {self.reduce!r}")
+        self.fused_reduce = self.reduce == "peer_store"
+        self.per_peer_streams = per_peer_streams
+        self.timeout_ms = timeout_ms
+        self._ce = None
+        self._epoch = 0
         # SMs left free for NCCL while the chunked GEMM2 runs (the persistent GEMM
         # otherwise holds every SM and the collectives cannot overlap it).
         self.comm_sms = comm_sms
@@ -59,11 +78,21 @@ class TensorParallelMLP:
 
     def _comm_stream(self, x):
         if x.is_cuda and self._comm is None:
-            self._comm = torch.cuda.Stream(device=x.device)
+            # high priority: the epilogue kernels between collectives go ahead of
+            # the next GEMM chunk's CTAs
+            self._comm = torch.cuda.Stream(device=x.device, priority=-1)
         return self._comm
 
-    def __call__(self, x):
-        """Forward on this rank (x replicated); returns the full [M, d] output."""
+    def __call__(self, x, out=None):
+        """Forward on this rank (x replicated); returns the full [M, d] output
+        (written into `out` when given)."""
+        y = self._forward(x, out)
+        if out is not None and y is not out:
+            out.copy_(y)
+            return out
+        return y
+
+    def _forward(self, x, out=None):
         k = self.kern
         xn = k.rmsnorm(x, self.gamma, self.eps)
         h = k.fused_matmul_bias_gelu(xn, self.w1, self.b1)
@@ -71,8 +100,10 @@ class TensorParallelMLP:
             y32 = k.matmul_f32out(h, self.w2)
             return k.bias_residual_f32(y32, self.b2, x)
         M = h.shape[0]
-        if self.fused_reduce and x.is_cuda:
+        if self.reduce == "peer_store" and x.is_cuda:
             return self._fused(x, h, M)
+        if self.reduce == "copy_engine" and x.is_cuda:
+            return self._copy_engine(x, h, M, out)
         if self.chunks == 1 or not x.is_cuda:
             y32 = k.matmul_f32out(h, self.w2)
             dist.all_reduce(y32, group=self.group)
@@ -161,3 +192,101 @@ class TensorParallelMLP:
             mine.data_ptr(), stream), "reduce_slots_bias_residual")
         dist.all_gather_into_tensor(out, mine, group=self.group)
         return out
+
+    # ------------------------------------------------------ copy-engine path --
+    def _ce_plan(self, x, M, d):
+        """Slot / row / flag buffers shared with the peers and the native plan,
+        built once per (M, d). The buffers are plain device allocations mapped
+        into the peers with CUDA IPC handles (no multicast object); the flags
+        start at zero on every rank before any rank can push."""
+        import ctypes
+
+        from ._lib import check, lib
+        key = (M, d, self.chunks)
+        if self._ce is not None and self._ce["key"] == key:
+            return self._ce
+        self.close()
+        W = self.world
+        rank = dist.get_rank(self.group)
+        C = self.chunks
+        rows = M // C
+        if rows * C != M or rows % W:
+            raise ValueError(f"M={M} must split into {C} chunks of a multiple of {W} rows")
+        per = rows // W
+        sizes = (C * W * per * d * 4, C * per * d * 2, (2 * C * W + 4) * 4)  # slots, rows, flags
+        own, handles = [], []
+        for nbytes in sizes:
+            p = ctypes.c_void_p()
+            hbuf = ctypes.create_string_buffer(64)
+            check(lib().pkb200_ipc_alloc(nbytes, ctypes.byref(p), hbuf), "ipc_alloc")
+            own.append(p.value)
+            handles.append(hbuf.raw)
+        gathered = [None] * W
+        dist.all_gather_object(gathered, handles, group=self.group)
+        opened = []
+        tables = []
+        for b in range(3):
+            ptrs = (ctypes.c_void_p * W)()
+            for p in range(W):
+                if p == rank:
+                    ptrs[p] = own[b]
+                    continue
+                q = ctypes.c_void_p()
+                check(lib().pkb200_ipc_open(gathered[p][b], ctypes.byref(q)), "ipc_open")
+                ptrs[p] = q.value
+                opened.append(q.value)
+            tables.append(ptrs)
+        y32 = torch.empty(M, d, dtype=torch.float32, device=x.device)
+        epoch_src = torch.zeros(2 * 8 + 2, dtype=torch.int32, device=x.device)
+        torch.cuda.synchronize(x.device)
+        dist.barrier(group=self.group)       # every rank's flags are zero and mapped
+        plan = ctypes.c_void_p()
+        check(lib().pkb200_tp_ce_create(W, rank, M, d, C, int(self.per_peer_streams),
+                                        y32.data_ptr(), tables[0], tables[1], tables[2],
+                                        epoch_src.data_ptr(), ctypes.byref(plan)),
+              "tp_ce_create")
+        self._ce = dict(key=key, plan=plan, own=own, opened=opened, keep=(tables, y32, epoch_src))
+        self._epoch = 0
+        return self._ce
+
+    def _copy_engine(self, x, h, M, out=None):
+        from ._lib import check, lib
+        d = self.w2.shape[1]
+        ce = self._ce_plan(x, M, d)
+        self._epoch += 1
+        if out is None:
+            out = torch.empty_like(x)
+        check(lib().pkb200_tp_ce_mlp_step(ce["plan"], h.data_ptr(), self.w2.data_ptr(), h.shape[1],
+                                          self.b2.data_ptr(), x.data_ptr(), out.data_ptr(),
+                                          self._epoch, torch.cuda.current_stream().cuda_stream),
+              "tp_ce_mlp_step")
+        return out
+
+    def wait(self, timeout_ms=None):
+        """Host wait for the last copy-engine step with a deadline; raises
+        TimeoutError (after releasing this rank's waits) when a peer did not
+        deliver in time."""
+        from ._lib import lib
+        if self._ce is None:
+            return
+        st = lib().pkb200_tp_ce_wait(self._ce["plan"], int(timeout_ms or self.timeout_ms))
+        if st != 0:
+            raise TimeoutError(f"tensor-parallel exchange did not complete (status {st})")
+
+    def close(self, collective=True):
+        """Release the copy-engine plan (streams, events) and its shared
+        buffers. With `collective` every rank calls it together: the barrier
+        keeps a buffer alive until no peer can still copy from it."""
+        if self._ce is not None:
+            from ._lib import lib
+            torch.cuda.synchronize()
+            if collective:
+                dist.barrier(group=self.group)
+            lib().pkb200_tp_ce_destroy(self._ce["plan"])
+            for p in self._ce["opened"]:
+                lib().pkb200_ipc_close(p)
+            if collective:
+                dist.barrier(group=self.group)
+            for p in self._ce["own"]:
+                lib().pkb200_free(p)
+            self._ce = None
