@@ -260,6 +260,10 @@ def run_gpu_arm(args):
         mlp = lambda xx, out: ops.mlp_block(xx, gamma, w1, b1, w2, b2, eps, ws, out)  # noqa
         launches_per_step = 3 + 1
     else:
+        if args.tp_mode == "auto":
+            # measured: the copy-engine exchange is faster at 2 ranks (2381 vs
+            # 2137 TFLOP/s), NCCL at 8 (4994 vs 4508); 4 ranks keep NCCL
+            args.tp_mode = "ce" if world == 2 else "nccl"
         reduce = {"fused": "peer_store", "nccl": "nccl", "ce": "copy_engine"}[args.tp_mode]
         tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks, reduce=reduce,
                                 per_peer_streams=not args.tp_one_stream)
@@ -510,9 +514,10 @@ def main():
     ap.add_argument("--tp-chunks", type=int, default=4)
     ap.add_argument("--tp-one-stream", action="store_true",
                     help="copy-engine exchange: one push and one pull stream for all peers")
-    ap.add_argument("--tp-mode", default="ce", choices=["ce", "fused", "nccl"],
-                    help="ce: chunked GEMM2, copy-engine push of the fp32 partials to their owners "
-                         "and pull of the reduced rows (default); nccl: chunked GEMM2 + NCCL "
+    ap.add_argument("--tp-mode", default="auto", choices=["auto", "ce", "fused", "nccl"],
+                    help="auto (default): ce at 2 ranks, nccl otherwise; "
+                         "ce: chunked GEMM2, copy-engine push of the fp32 partials to their owners "
+                         "and pull of the reduced rows; nccl: chunked GEMM2 + NCCL "
                          "reduce-scatter/all-gather; fused: GEMM2 epilogue stores partials into "
                          "the owners' buffers over NVLink")
     ap.add_argument("--e2e-chunks", type=int, default=8,
