@@ -341,12 +341,18 @@ def run_gpu_arm(args):
     attn_ms = time_attention()
 
     # End to end through the public API with HOST buffers: pinned host X/Q/K/V
-    # in, this rank's Y rows and O out, every step. The MLP streams row chunks
+    # in, Y and O out, every step. The MLP streams row chunks
     # (polykernel_b200.streaming.HostStreamed) so the copies overlap compute.
+    # With N ranks each rank moves only its own M/N rows of X and Y across
+    # PCIe: per streamed chunk the ranks all-gather their X rows over NVLink,
+    # run the tensor-parallel block on the gathered rows, and each keeps its
+    # own rows of the result. Attention is head-sharded, so each rank copies
+    # its own heads. The byte counts below are per rank.
     from polykernel_b200.streaming import HostStreamed
-    xh = x.cpu().pin_memory()
+    r_lo, r_hi = (M * rank) // world, (M * (rank + 1)) // world
+    xh = x[r_lo:r_hi].cpu().pin_memory()
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, kn, vn))
-    yh = torch.empty(M, d, dtype=bf).pin_memory()
+    yh = torch.empty(r_hi - r_lo, d, dtype=bf).pin_memory()
     oh = torch.empty_like(o, device="cpu").pin_memory()
     # two device sets for Q/K/V, so the next step's copies need not wait for
     # this step's attention
@@ -356,9 +362,19 @@ def run_gpu_arm(args):
         ws_c = ops.mlp_workspace(-(-M // args.e2e_chunks), d, ffn, dev)
         fwd = lambda xx, out: ops.mlp_block(xx, gamma, w1, b1, w2, b2, eps, ws_c, out)  # noqa
     else:
-        fwd = lambda xx, out: tpm(xx, out=out)  # noqa
+        gather_bufs = {}
+
+        def fwd(xx, out):
+            n = xx.shape[0]
+            if n not in gather_bufs:
+                gather_bufs[n] = (torch.empty(world * n, d, dtype=bf, device=dev),
+                                  torch.empty(world * n, d, dtype=bf, device=dev))
+            xg, yg = gather_bufs[n]
+            dist.all_gather_into_tensor(xg, xx)       # rows are rank-major: [rank][n]
+            tpm(xg, out=yg)
+            out.copy_(yg[rank * n:(rank + 1) * n])    # the block is row-independent
+            return out
     streamer = HostStreamed(fwd, chunks=args.e2e_chunks)
-    r_lo, r_hi = (M * rank) // world, (M * (rank + 1)) // world
 
     o_read = [None]  # device->host copy of the previous step's O done (o is free)
     step_no = [0]
@@ -402,6 +418,9 @@ def run_gpu_arm(args):
 
     e2e_step()
     e2e_join()
+    torch.cuda.synchronize()
+    # the host-buffer path computes the same rows as the device-resident step
+    e2e_rows_exact = (yh == y[r_lo:r_hi].cpu()).float().mean().item()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -413,10 +432,7 @@ def run_gpu_arm(args):
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     h2d = (xh.numel() + qh.numel() + kh.numel() + vh.numel()) * 2
-    # every rank copies the full Y back (it holds it after the all-gather); only
-    # this rank's rows are new information, but all bytes cross PCIe
     d2h = (yh.numel() + oh.numel()) * 2
-    del r_lo, r_hi
 
     def gmax(v):
         if world == 1:
@@ -528,7 +544,8 @@ def run_gpu_arm(args):
                          "traffic": args.traffic},
             "cpu_baseline": cpu,
             "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "bytes_scope": "per rank", "rows_bit_exact_vs_device_step": e2e_rows_exact},
             "gpu_launches": launches_per_step * args.steps,
             "other_configs": others,
             "clocks": clocks,
