@@ -457,12 +457,13 @@ def run_gpu_arm(args):
     # The other BASELINE configs on one GPU (informational; not part of `value`).
     others = None
     if world == 1 and not args.no_others:
-        others = {}
+        others = {"timed": "each alone after 2 s idle (burst clocks)"}
 
         def tflops_of(fn, flops, iters=10):
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()
+            time.sleep(2.0)     # let the clocks recover from the previous measurement
             a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a_.record(stream)
             for _ in range(iters):
@@ -578,8 +579,8 @@ def main():
     ap.add_argument("--no-others", action="store_true",
                     help="skip the informational config-2/3/4 measurements")
     # DRAM bytes per config-5 GEMM1 launch: 1.71 GB measured by ncu at M=4096
-    # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).
-    ap.add_argument("--traffic", type=float, default=6.83e9,
+    # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md: 1.80 GB) x 4 for M=16384 (traffic grows with M).
+    ap.add_argument("--traffic", type=float, default=7.19e9,
                     help="DRAM bytes per GEMM1 launch from an ncu capture (scaled)")
     args = ap.parse_args()
     if args.warmup < 3:
