@@ -324,6 +324,29 @@ void launch_kv_cache_update(const __nv_bfloat16* cache, const __nv_bfloat16* new
                             void* stream);
 void launch_matmul_int8(const __nv_bfloat16* A, const int8_t* Wq, const float* scale,
                         __nv_bfloat16* C, int M, int N, int K, void* stream);
+
+/* Additive entries in the same style (new; the reference composes these
+ * chains from the kernels above and golden primitives, tests/e2e/conftest.py:
+ * 104-107): RMSNorm with gamma fused into the GEMM (golden.py:96-100), the
+ * whole MLP block and its int8 weight-only variant (library-owned workspace),
+ * and prefill attention appending the new K/V rows in place into a
+ * preallocated [B, H, S_max, D] cache. */
+void launch_fused_rmsnorm_matmul_gamma(const __nv_bfloat16* input, const __nv_bfloat16* weight,
+                                       const __nv_bfloat16* gamma, __nv_bfloat16* output, int M,
+                                       int N, int K, float epsilon, void* stream);
+void launch_mlp_block(const __nv_bfloat16* X, const __nv_bfloat16* gamma,
+                      const __nv_bfloat16* W1, const __nv_bfloat16* b1, const __nv_bfloat16* W2,
+                      const __nv_bfloat16* b2, __nv_bfloat16* Y, int M, int d, int ffn, float eps,
+                      void* stream);
+void launch_mlp_block_int8(const __nv_bfloat16* X, const __nv_bfloat16* gamma,
+                           const int8_t* W1q, const float* s1, const __nv_bfloat16* b1,
+                           const int8_t* W2q, const float* s2, const __nv_bfloat16* b2,
+                           __nv_bfloat16* Y, int M, int d, int ffn, float eps, void* stream);
+void launch_attention_prefill_kv_append(const __nv_bfloat16* Q, const __nv_bfloat16* K_new,
+                                        const __nv_bfloat16* V_new, __nv_bfloat16* K_cache,
+                                        __nv_bfloat16* V_cache, __nv_bfloat16* O, int B, int H,
+                                        int S_q, int S_cache, int S_max, int D, float scale,
+                                        int causal, void* stream);
 #endif
 
 #endif /* PKB200_H */

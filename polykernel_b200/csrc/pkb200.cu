@@ -114,15 +114,17 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // --------------------------------------------------------------- workspace --
 // Grow-only device scratch owned by the library, one buffer per (device,
 // stream), for the entry points whose reference signature has no workspace
-// argument (launch_fused_rmsnorm_matmul, launch_matmul_int8).
-std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_ws;
+// argument (launch_fused_rmsnorm_matmul, launch_matmul_int8). A second pool
+// holds the block workspace the launch_mlp_block* wrappers hand to
+// pkb200_mlp_block*, whose steps may use the first pool themselves.
+std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_ws, g_ws_block;
 
-int library_workspace(size_t bytes, cudaStream_t s, void** out) {
+int library_workspace(size_t bytes, cudaStream_t s, void** out, bool block_pool = false) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lk(g_mu);
-  auto& slot = g_ws[{dev, s}];
+  auto& slot = (block_pool ? g_ws_block : g_ws)[{dev, s}];
   if (slot.second < bytes) {
     if (slot.first) {
       e = cudaStreamSynchronize(s);
@@ -1545,4 +1547,41 @@ void launch_kv_cache_update(const bf16* cache, const bf16* new_rows, bf16* out, 
 void launch_matmul_int8(const bf16* A, const int8_t* Wq, const float* scale, bf16* C, int M, int N,
                         int K, void* stream) {
   report("launch_matmul_int8", pkb200_matmul_int8(A, Wq, scale, C, M, N, K, stream));
+}
+
+// Additive entries in the same style (void return, errors printed): the
+// chains the reference composes from its kernels, as single calls.
+void launch_fused_rmsnorm_matmul_gamma(const bf16* input, const bf16* weight, const bf16* gamma,
+                                       bf16* output, int M, int N, int K, float epsilon,
+                                       void* stream) {
+  report("launch_fused_rmsnorm_matmul_gamma",
+         pkb200_fused_rmsnorm_matmul(input, weight, gamma, output, M, N, K, epsilon, stream));
+}
+void launch_mlp_block(const bf16* X, const bf16* gamma, const bf16* W1, const bf16* b1,
+                      const bf16* W2, const bf16* b2, bf16* Y, int M, int d, int ffn, float eps,
+                      void* stream) {
+  const size_t bytes = pkb200_mlp_block_workspace_size(M, d, ffn);
+  void* ws = nullptr;
+  int e = M <= 0 ? 0 : library_workspace(bytes, S(stream), &ws, true);
+  if (!e) e = pkb200_mlp_block(X, gamma, W1, b1, W2, b2, Y, M, d, ffn, eps, ws, bytes, stream);
+  report("launch_mlp_block", e);
+}
+void launch_mlp_block_int8(const bf16* X, const bf16* gamma, const int8_t* W1q, const float* s1,
+                           const bf16* b1, const int8_t* W2q, const float* s2, const bf16* b2,
+                           bf16* Y, int M, int d, int ffn, float eps, void* stream) {
+  const size_t bytes = pkb200_mlp_block_workspace_size(M, d, ffn);
+  void* ws = nullptr;
+  int e = M <= 0 ? 0 : library_workspace(bytes, S(stream), &ws, true);
+  if (!e)
+    e = pkb200_mlp_block_int8(X, gamma, W1q, s1, b1, W2q, s2, b2, Y, M, d, ffn, eps, ws, bytes,
+                              stream);
+  report("launch_mlp_block_int8", e);
+}
+void launch_attention_prefill_kv_append(const bf16* Q, const bf16* K_new, const bf16* V_new,
+                                        bf16* K_cache, bf16* V_cache, bf16* O, int B, int H,
+                                        int S_q, int S_cache, int S_max, int D, float scale,
+                                        int causal, void* stream) {
+  report("launch_attention_prefill_kv_append",
+         pkb200_attention_prefill_kv_append(Q, K_new, V_new, K_cache, V_cache, O, B, H, S_q,
+                                            S_cache, S_max, D, scale, causal, stream));
 }

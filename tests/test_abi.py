@@ -56,6 +56,12 @@ def test_reference_mangled_names_exact():
               "_Z14launch_rmsnormPK13__nv_bfloat16S1_PS_iifPv",
               "_Z11launch_geluPK13__nv_bfloat16PS_iPv"):
         assert m in syms, m
+    # the additive entries, in the same style
+    for m in ("_Z33launch_fused_rmsnorm_matmul_gammaPK13__nv_bfloat16S1_S1_PS_iiifPv",
+              "_Z16launch_mlp_blockPK13__nv_bfloat16S1_S1_S1_S1_S1_PS_iiifPv",
+              "_Z21launch_mlp_block_int8PK13__nv_bfloat16S1_PKaPKfS1_S3_S5_S1_PS_iiifPv",
+              "_Z34launch_attention_prefill_kv_appendPK13__nv_bfloat16S1_S1_PS_S2_S2_iiiiiifiPv"):
+        assert m in syms, m
 
 
 def test_workspace_size_is_host_only():

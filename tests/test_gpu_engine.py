@@ -60,3 +60,51 @@ def test_host_streamed_matches_device_and_pipelines_across_calls():
     torch.cuda.synchronize()
     for y, r in zip(yh, refs):
         assert torch.equal(y, r.cpu())
+
+
+def test_additive_launch_entries_match_c_abi():
+    """launch_mlp_block / launch_fused_rmsnorm_matmul_gamma /
+    launch_attention_prefill_kv_append (reference-style C++ symbols, library
+    workspace) give the same bits as the C ABI calls they wrap."""
+    import torch
+
+    import polykernel_b200 as pk
+    from polykernel_b200._lib import lib
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    L = lib()
+    P = ctypes.c_void_p
+    g = torch.Generator(device="cuda").manual_seed(9)
+    M, d, ffn = 256, 512, 1024
+    X = torch.randn(M, d, device="cuda", generator=g).bfloat16()
+    gm = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    w1 = (torch.randn(d, ffn, device="cuda", generator=g) / 22).bfloat16()
+    b1 = (0.02 * torch.randn(ffn, device="cuda", generator=g)).bfloat16()
+    w2 = (torch.randn(ffn, d, device="cuda", generator=g) / 32).bfloat16()
+    b2 = (0.02 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    s = torch.cuda.current_stream().cuda_stream
+    y = torch.empty_like(X)
+    fn = getattr(L, "_Z16launch_mlp_blockPK13__nv_bfloat16S1_S1_S1_S1_S1_PS_iiifPv")
+    fn.restype = None
+    fn(*[P(t.data_ptr()) for t in (X, gm, w1, b1, w2, b2, y)], M, d, ffn, ctypes.c_float(1e-6),
+       P(s))
+    assert torch.equal(y, pk.ops.mlp_block(X, gm, w1, b1, w2, b2, 1e-6))
+    out = torch.empty(M, ffn, dtype=torch.bfloat16, device="cuda")
+    fn = getattr(L, "_Z33launch_fused_rmsnorm_matmul_gammaPK13__nv_bfloat16S1_S1_PS_iiifPv")
+    fn.restype = None
+    fn(P(X.data_ptr()), P(w1.data_ptr()), P(gm.data_ptr()), P(out.data_ptr()), M, ffn, d,
+       ctypes.c_float(1e-6), P(s))
+    assert torch.equal(out, pk.ops.fused_rmsnorm_matmul(X, w1, gm, 1e-6))
+    B, H, S, D, Smax = 1, 2, 160, 64, 256
+    q, kn, vn = (torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16() for _ in range(3))
+    kc = torch.zeros(B, H, Smax, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    o = torch.empty_like(q)
+    fn = getattr(L, "_Z34launch_attention_prefill_kv_appendPK13__nv_bfloat16S1_S1_PS_S2_S2_iiiiiifiPv")
+    fn.restype = None
+    fn(*[P(t.data_ptr()) for t in (q, kn, vn, kc, vc, o)], B, H, S, 0, Smax, D,
+       ctypes.c_float(D ** -0.5), 1, P(s))
+    kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+    o2 = pk.ops.attention_prefill_kv_append(q, kn, vn, kc2, vc2, 0, True)
+    assert torch.equal(o, o2) and torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert pk.device_error() == 0
