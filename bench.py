@@ -114,37 +114,101 @@ def synthetic_host_weights(M, d, ffn, seed=0):
     return x, gamma, w1, b1, w2, b2
 
 
+REF_ATTN = os.path.join(ROOT, "oracle", "_ref", "attention")
+
+
+def write_npy_bf16(path, bits):
+    """bf16 bits as a '<V2' .npy (the reference's npy_io format)."""
+    import numpy as np
+    np.save(path, np.ascontiguousarray(bits, dtype=np.uint16).view("V2"))
+
+
 def run_reference_arm(args):
-    """--impl reference: the reference's CPU MLP chain, bounded row sample per step."""
+    """--impl reference: the reference's own CPU code for the whole step, on a
+    bounded sample per step. Half the host threads run its MLP chain
+    (ref_mlp_rows: launch_rmsnorm_cpu -> launch_fused_matmul_bias_gelu_cpu ->
+    launch_matmul_cpu + bias/add, one token row each), the other half its
+    causal prefill attention binary (kernels/cpu/attention.cpp `prefill`, one
+    (batch, head) each), at the same time. Rows and heads are independent, so
+    the full config-5 MLP + config-3 attention step is extrapolated from the
+    per-row and per-head core-seconds onto all threads."""
+    import numpy as np
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cfg = MLP_CFG
-    if not os.path.exists(REF_LIB):
+    cfg, acfg = MLP_CFG, ATTN_CFG
+    missing = [f for f in (REF_LIB, REF_ATTN) if not os.path.exists(f)]
+    if missing:
         print(json.dumps({"impl": "reference", "unavailable":
-                          "oracle/_ref/liboracle_ref.so not built (make -C oracle)"}))
+                          f"{', '.join(os.path.relpath(m, ROOT) for m in missing)} not built "
+                          "(make -C oracle)"}))
         return 0
     threads = host_threads()
-    # rows in the sample: one row per thread per step (~3.5 s per row per core at config 5)
-    sample_rows = threads
-    x, gamma, w1, b1, w2, b2 = synthetic_host_weights(sample_rows, cfg["d"], cfg["ffn"])
-    times = []
-    for i in range(args.warmup + args.steps):
-        _, dt, rows = cpu_mlp_rows_tflops(x, gamma, w1, b1, w2, b2, 1, threads)
-        if i >= args.warmup:
-            times.append(dt)
-    tot = sum(times)
-    flops = mlp_flops(sample_rows, cfg["d"], cfg["ffn"]) * len(times)
-    value = flops / tot / 1e12
-    sample = (f"{sample_rows} of {cfg['M']} token rows of the config-5 MLP block per step "
-              f"(work is linear in rows); attention part not run on CPU")
+    t_mlp = max(1, threads // 2)
+    t_att = max(1, threads - t_mlp)
+    x, gamma, w1, b1, w2, b2 = synthetic_host_weights(t_mlp, cfg["d"], cfg["ffn"])
+    rng = np.random.default_rng(1)
+    S, D = acfg["S"], acfg["D"]
+    tmp = tempfile.mkdtemp(prefix="pkb200_ref_")
+
+    def bf(a):
+        u = np.ascontiguousarray(a.astype(np.float32)).view(np.uint32)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    heads = []
+    for h in range(t_att):
+        paths = [os.path.join(tmp, f"{n}{h}.npy") for n in ("q", "k", "v", "o")]
+        for pth in paths[:3]:
+            write_npy_bf16(pth, bf(rng.standard_normal((1, 1, S, D), dtype=np.float32)))
+        heads.append(paths)
+
+    def attention_group():
+        procs = [subprocess.Popen([REF_ATTN, "prefill", *hp, "--causal", "1"],
+                                  stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                 for hp in heads]
+        return [pr.wait() for pr in procs]
+
+    per_row, per_head = [], []
+    try:
+        for i in range(args.warmup + args.steps):
+            res = {}
+
+            def att():
+                t0 = time.perf_counter()
+                res["rc"] = attention_group()
+                res["att"] = time.perf_counter() - t0
+            th = threading.Thread(target=att)
+            th.start()
+            _, dt_mlp, _ = cpu_mlp_rows_tflops(x, gamma, w1, b1, w2, b2, 1, t_mlp)
+            th.join()
+            if any(res["rc"]):
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "reference attention binary failed"}))
+                return 0
+            if i >= args.warmup:
+                per_row.append(dt_mlp)       # core-seconds per token row
+                per_head.append(res["att"])  # core-seconds per (batch, head)
+    finally:
+        import shutil
+        shutil.rmtree(tmp, ignore_errors=True)
+    BH = acfg["B"] * acfg["H"]
+    step_s = (statistics.mean(per_row) * cfg["M"] + statistics.mean(per_head) * BH) / threads
+    flops = mlp_flops(cfg["M"], cfg["d"], cfg["ffn"]) + attn_flops(acfg["B"], acfg["H"], S, D)
+    value = flops / step_s / 1e12
+    sample = (f"per step {t_mlp} of {cfg['M']} token rows of the config-5 MLP block and {t_att} "
+              f"of {BH} (batch, head) pairs of config-3 causal prefill, concurrently on "
+              f"{threads} host threads; the full step is extrapolated (rows and heads are "
+              f"independent). The KV append is a copy of the new rows (S_cache=0) and is not timed")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * tot / len(times), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config-5 distributions)",
-        "config": {"workload": "config5_mlp_block_rows", "M_sample": sample_rows, "d": cfg["d"],
-                   "ffn": cfg["ffn"], "parallelism": f"{threads} host threads"},
+        "ms_per_step": 1e3 * step_s, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config-5 / config-3 shapes and distributions)",
+        "config": {"workload": "config5_mlp_block+config3_attention_prefill_kv_append",
+                   "mlp": {"M": cfg["M"], "d": cfg["d"], "ffn": cfg["ffn"]},
+                   "attention": {"B": acfg["B"], "H": acfg["H"], "S": S, "D": D, "S_cache": 0,
+                                 "cache_rows": acfg["S_max"]},
+                   "parallelism": f"{threads} host threads"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -578,8 +642,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-others", action="store_true",
                     help="skip the informational config-2/3/4 measurements")
-    # DRAM bytes per config-5 GEMM1 launch: 1.71 GB measured by ncu at M=4096
-    # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md: 1.80 GB) x 4 for M=16384 (traffic grows with M).
+    # DRAM bytes per config-5 GEMM1 launch: 1.80 GB measured by ncu at M=4096
+    # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).
     ap.add_argument("--traffic", type=float, default=7.19e9,
                     help="DRAM bytes per GEMM1 launch from an ncu capture (scaled)")
     args = ap.parse_args()
