@@ -46,7 +46,7 @@ class ConfigSpace:
     @staticmethod
     def smem_bytes(c):
         stage = c["block_m"] * c["block_k"] * 2 + c["block_k"] * c["block_n"] * 2
-        return c["shared_memory_stages"] * stage + 1024 + 256
+        return c["shared_memory_stages"] * stage + 1024 + 512  # + alignment, barriers/tile ring
 
     @classmethod
     def prune_reason(cls, c):
@@ -202,10 +202,16 @@ def _metrics(a, r):
     return {"cosine": cos, "max_rel_err": rel, "pcc": pcc}
 
 
-def autotune(op, M, N, K, iters=10, warmup=3, seed=0):
+def autotune(op, M, N, K, iters=10, warmup=3, seed=0, inject_broken=False, report=None):
     """Time every ConfigSpace config for `op` at (M, N, K) on the current GPU and
     return cache entries (one per op/shape: the fastest validated config).
-    Ops: matmul, fused_matmul_bias_gelu, matmul_bias_residual."""
+    Ops: matmul, fused_matmul_bias_gelu, matmul_bias_residual.
+
+    `inject_broken` adds a fast-but-wrong candidate (it only fills the output),
+    the negative path of the reference's autotuner (tools/polykernel-bench/
+    bench.py `--inject-broken`): the correctness gate must reject it although
+    it is the fastest. `report`, when a list, receives one dict per candidate
+    (label, time_ms, validated, metrics)."""
     import torch
 
     from . import ops
@@ -223,29 +229,37 @@ def autotune(op, M, N, K, iters=10, warmup=3, seed=0):
         ref32 = torch.nn.functional.gelu(ref32 + bias.float())
     elif op == "matmul_bias_residual":
         ref32 = ref32 + bias.float() + resid.float()
+    broken_out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    candidates = [(f"block_n={c['block_n']},stages={c['shared_memory_stages']}", c, run)
+                  for c in ConfigSpace.enumerate()]
+    if inject_broken:
+        candidates.append(("broken", None, lambda: broken_out.fill_(0.5)))
     results = []
     try:
         lib().pkb200_set_gemm_config(_cfg_array(DEFAULT))
         base = run()
-        for cfg in ConfigSpace.enumerate():
-            if lib().pkb200_set_gemm_config(_cfg_array(cfg)) != 0:
+        for label, cfg, fn in candidates:
+            if cfg is not None and lib().pkb200_set_gemm_config(_cfg_array(cfg)) != 0:
                 continue
-            out = run()
+            out = fn()
             torch.cuda.synchronize()
             m = _metrics(out.float(), ref32)
             ok = bool(torch.equal(out, base)) and m["cosine"] >= 0.999 and m["pcc"] >= 0.99
             for _ in range(warmup):
-                run()
+                fn()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             for _ in range(iters):
-                run()
+                fn()
             e.record()
             torch.cuda.synchronize()
-            results.append((s.elapsed_time(e) / iters, ok, cfg, m))
+            t = s.elapsed_time(e) / iters
+            results.append((t, ok, cfg, m))
+            if report is not None:
+                report.append({"label": label, "time_ms": t, "validated": ok, "metrics": m})
     finally:
         lib().pkb200_set_gemm_config(None)
-    valid = [r for r in results if r[1]]
+    valid = [r for r in results if r[1] and r[2] is not None]
     if not valid:
         return []
     t, _, cfg, m = min(valid, key=lambda r: r[0])

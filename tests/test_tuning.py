@@ -160,3 +160,18 @@ def test_every_compiled_variant_matches_default(cuda, bn, stages):
             lib().pkb200_set_gemm_config(None)
         assert torch.equal(out, ref), (bn, stages, M, N, K)
     assert pk.device_error() == 0
+
+
+@pytest.mark.gpu
+def test_autotune_rejects_injected_broken_variant(cuda):
+    """Negative path (the reference autotuner's --inject-broken): a candidate
+    that only fills its output is the fastest, yet the correctness gate rejects
+    it and the cache entry names a real tcgen05 config."""
+    report = []
+    entries = T.autotune("matmul", 2048, 2048, 2048, iters=5, warmup=2, inject_broken=True,
+                         report=report)
+    broken = [r for r in report if r["label"] == "broken"]
+    assert broken and not broken[0]["validated"]
+    assert broken[0]["time_ms"] <= min(r["time_ms"] for r in report)
+    assert len(entries) == 1 and entries[0]["validated"]
+    assert (entries[0]["best"]["block_n"], entries[0]["best"]["shared_memory_stages"]) in T.COMPILED
