@@ -955,19 +955,26 @@ int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_p
   int lo = 0, hi = 0;
   cudaDeviceGetStreamPriorityRange(&lo, &hi);
   pl->nstreams = per_peer_streams ? world : 1;
-  for (int i = 0; i < pl->nstreams; ++i) {
-    if ((e = cudaStreamCreateWithFlags(&pl->push[i], cudaStreamNonBlocking))) return e;
-    if ((e = cudaStreamCreateWithFlags(&pl->pull[i], cudaStreamNonBlocking))) return e;
+  auto make = [&]() -> int {
+    int r;
+    for (int i = 0; i < pl->nstreams; ++i) {
+      if ((r = cudaStreamCreateWithFlags(&pl->push[i], cudaStreamNonBlocking))) return r;
+      if ((r = cudaStreamCreateWithFlags(&pl->pull[i], cudaStreamNonBlocking))) return r;
+    }
+    // the reduce kernels go ahead of the next GEMM chunk's CTAs when SMs free up
+    if ((r = cudaStreamCreateWithPriority(&pl->red, cudaStreamNonBlocking, hi))) return r;
+    if ((r = cudaStreamCreateWithFlags(&pl->release, cudaStreamNonBlocking))) return r;
+    for (int i = 0; i < chunks; ++i)
+      if ((r = cudaEventCreateWithFlags(&pl->ev_gemm[i], cudaEventDisableTiming))) return r;
+    for (int i = 0; i < 2 * kMaxPeers + 1; ++i)
+      if ((r = cudaEventCreateWithFlags(&pl->ev_end[i], cudaEventDisableTiming))) return r;
+    if ((r = cudaEventCreateWithFlags(&pl->ev_step, cudaEventDisableTiming))) return r;
+    return cudaEventCreateWithFlags(&pl->ev_done, cudaEventDisableTiming);
+  };
+  if ((e = make())) {
+    pkb200_tp_ce_destroy(pl.release());  // frees whatever was created
+    return e;
   }
-  // the reduce kernels go ahead of the next GEMM chunk's CTAs when SMs free up
-  if ((e = cudaStreamCreateWithPriority(&pl->red, cudaStreamNonBlocking, hi))) return e;
-  if ((e = cudaStreamCreateWithFlags(&pl->release, cudaStreamNonBlocking))) return e;
-  for (int i = 0; i < chunks; ++i)
-    if ((e = cudaEventCreateWithFlags(&pl->ev_gemm[i], cudaEventDisableTiming))) return e;
-  for (int i = 0; i < 2 * kMaxPeers + 1; ++i)
-    if ((e = cudaEventCreateWithFlags(&pl->ev_end[i], cudaEventDisableTiming))) return e;
-  if ((e = cudaEventCreateWithFlags(&pl->ev_step, cudaEventDisableTiming))) return e;
-  if ((e = cudaEventCreateWithFlags(&pl->ev_done, cudaEventDisableTiming))) return e;
   *plan_out = pl.release();
   return cudaSuccess;
 }
@@ -996,7 +1003,11 @@ int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_sha
   if (!pl || !h || !w2 || !b2 || !x || !out || ffn_shard <= 0) return cudaErrorInvalidValue;
   if (pl->aborted) return cudaErrorLaunchFailure;
   if (epoch == 0 || static_cast<int>(epoch - pl->last_epoch) <= 0) return cudaErrorInvalidValue;
-  return tp_ce_step(pl, cb(h), cb(w2), ffn_shard, cb(b2), cb(x), b(out), epoch, S(stream));
+  const int e = tp_ce_step(pl, cb(h), cb(w2), ffn_shard, cb(b2), cb(x), b(out), epoch, S(stream));
+  // a step that failed half-way may have left flag waits queued on the side
+  // streams that no peer will satisfy: the plan is not reused
+  if (e) pl->aborted = true;
+  return e;
 }
 
 int pkb200_tp_ce_wait(void* plan, int timeout_ms) {
