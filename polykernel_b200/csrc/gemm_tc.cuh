@@ -121,6 +121,10 @@ __device__ __forceinline__ uint4 epilogue8(const float (&acc)[8], const Epilogue
     const float4 s1 = __ldg(reinterpret_cast<const float4*>(ea.col_scale + n + 4));
     v[0] = acc[0] * s0.x; v[1] = acc[1] * s0.y; v[2] = acc[2] * s0.z; v[3] = acc[3] * s0.w;
     v[4] = acc[4] * s1.x; v[5] = acc[5] * s1.y; v[6] = acc[6] * s1.z; v[7] = acc[7] * s1.w;
+  } else {
+    // kinds whose tiles never reach this packer (fp32 and peer-store outputs)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = acc[j];
   }
   uint4 out;
   out.x = pack_bf16x2(v[0], v[1]);
