@@ -1,5 +1,5 @@
 /* pkb200.h - C ABI of libpkb200.so, the B200 (sm_100a) kernel library that
- * replaces the reference's kernels/generated/*.cu launch entry points.
+ * replaces the reference's kernels/generated/<op>.cu launch entry points.
  *
  * Conventions shared by every entry point:
  *   - bf16 tensors are raw 16-bit brain-float values (the reference's pk_bf16 /
@@ -303,7 +303,7 @@ int pkb200_path_counters(long long* out, int n);
 } /* extern "C" */
 
 /* ---- reference-compatible C++ entry points (same names, argument order and
- * void return as kernels/generated/*.cu; errors are printed to stderr). */
+ * void return as kernels/generated/<op>.cu; errors are printed to stderr). */
 #include <cuda_bf16.h>
 void launch_rmsnorm(const __nv_bfloat16* input, const __nv_bfloat16* weight,
                     __nv_bfloat16* output, int rows, int cols, float epsilon, void* stream);

@@ -13,6 +13,7 @@
 #pragma once
 
 #include <cctype>
+#include <cstdio>
 #include <cstdlib>
 #include <map>
 #include <memory>
@@ -172,6 +173,10 @@ struct Entry {
   long long M = 0, N = 0, K = 0;
   Config best;
   bool validated = false;
+  std::string scored_by = "measure";  // "measure" | "compile_time_model"
+  bool has_time = true;               // time_ms is null iff scored by the model
+  double time_ms = 0;
+  double cosine = 0, max_rel_err = 0, pcc = 0;
 };
 
 inline bool expect_keys(const Json& o, const std::set<std::string>& keys, const std::string& where,
@@ -204,12 +209,14 @@ inline bool get_int(const Json& o, const char* k, long long& out, const std::str
   return true;
 }
 
-inline bool get_num(const Json& o, const char* k, const std::string& where, std::string& err) {
+inline bool get_num(const Json& o, const char* k, const std::string& where, std::string& err,
+                    double* out = nullptr) {
   const Json* v = o.get(k);
   if (!v || v->kind != Json::Num) {
     err = where + "." + k + ": expected a number";
     return false;
   }
+  if (out) *out = v->num;
   return true;
 }
 
@@ -283,6 +290,9 @@ inline bool parse_cache(const std::string& text, std::vector<Entry>& out, std::s
       err = w + ".time_ms: null iff scored_by is \"compile_time_model\"";
       return false;
     }
+    ent.scored_by = scored;
+    ent.has_time = tm->kind == Json::Num;
+    ent.time_ms = ent.has_time ? tm->num : 0;
     const Json* val = e.get("validated");
     if (val->kind != Json::Bool) {
       err = w + ".validated: expected a boolean";
@@ -291,13 +301,75 @@ inline bool parse_cache(const std::string& text, std::vector<Entry>& out, std::s
     ent.validated = val->b;
     const Json& c = *e.get("correctness");
     if (!expect_keys(c, {"cosine", "max_rel_err", "pcc"}, w + ".correctness", err)) return false;
-    if (!get_num(c, "cosine", w + ".correctness", err) ||
-        !get_num(c, "max_rel_err", w + ".correctness", err) ||
-        !get_num(c, "pcc", w + ".correctness", err))
+    if (!get_num(c, "cosine", w + ".correctness", err, &ent.cosine) ||
+        !get_num(c, "max_rel_err", w + ".correctness", err, &ent.max_rel_err) ||
+        !get_num(c, "pcc", w + ".correctness", err, &ent.pcc))
       return false;
     out.push_back(ent);
   }
   return true;
+}
+
+// ------------------------------------------------------------ serializer --
+inline std::string json_string(const std::string& v) {
+  std::string o = "\"";
+  for (const char c : v) {
+    switch (c) {
+      case '"': o += "\\\""; break;
+      case '\\': o += "\\\\"; break;
+      case '\n': o += "\\n"; break;
+      case '\t': o += "\\t"; break;
+      case '\r': o += "\\r"; break;
+      default:
+        if (static_cast<unsigned char>(c) < 0x20) {
+          char buf[8];
+          std::snprintf(buf, sizeof(buf), "\\u%04x", static_cast<unsigned char>(c));
+          o += buf;
+        } else {
+          o += c;
+        }
+    }
+  }
+  return o + "\"";
+}
+
+inline std::string json_number(double v) {
+  char buf[40];
+  std::snprintf(buf, sizeof(buf), "%.17g", v);
+  std::string s(buf);
+  // keep it a JSON number that parses back as non-integer when it was one
+  if (s.find_first_of(".eEn") == std::string::npos) s += ".0";
+  return s;
+}
+
+inline std::string shape_json(const Entry& e) {
+  return "{\"M\": " + std::to_string(e.M) + ", \"N\": " + std::to_string(e.N) +
+         ", \"K\": " + std::to_string(e.K) + ", \"dtype\": " + json_string(e.dtype) + "}";
+}
+
+// A cache document in the schema parse_cache reads (version 1).
+inline std::string serialize_cache(const std::vector<Entry>& entries) {
+  std::string o = "{\n  \"version\": 1,\n  \"entries\": [";
+  for (size_t i = 0; i < entries.size(); ++i) {
+    const Entry& e = entries[i];
+    const Config& b = e.best;
+    o += i ? ",\n    {" : "\n    {";
+    o += "\"gpu\": " + json_string(e.gpu) + ", \"op\": " + json_string(e.op) +
+         ", \"shape\": " + shape_json(e) + ", \"best\": {\"block_m\": " +
+         std::to_string(b.block_m) + ", \"block_n\": " + std::to_string(b.block_n) +
+         ", \"block_k\": " + std::to_string(b.block_k) + ", \"num_warps\": " +
+         std::to_string(b.num_warps) + ", \"vector_width\": " + std::to_string(b.vector_width) +
+         ", \"unroll\": " + std::to_string(b.unroll) + ", \"shared_memory_stages\": " +
+         std::to_string(b.shared_memory_stages) + "}, \"scored_by\": " +
+         json_string(e.scored_by) + ", \"time_ms\": " +
+         (e.has_time ? json_number(e.time_ms) : std::string("null")) +
+         ", \"validated\": " + (e.validated ? "true" : "false") +
+         ", \"correctness\": {\"cosine\": " + json_number(e.cosine) +
+         ", \"max_rel_err\": " + json_number(e.max_rel_err) + ", \"pcc\": " +
+         json_number(e.pcc) + "}}";
+  }
+  o += entries.empty() ? "]\n}\n" : "\n  ]\n}\n";
+  return o;
 }
 
 }  // namespace tuning

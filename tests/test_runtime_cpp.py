@@ -1,0 +1,30 @@
+"""CPU: the C++ runtime (include/pkb200_runtime.h) built with g++ against
+libpkb200.so and run GPU-free (tests/cpp/runtime_test.cpp)."""
+import os
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIBDIR = os.path.join(ROOT, "polykernel_b200", "_lib")
+CUDA_INC = "/usr/local/cuda/include"
+CUDA_LIB = "/usr/local/cuda/lib64"
+
+
+def test_cpp_runtime(tmp_path):
+    if shutil.which("g++") is None:
+        pytest.skip("g++ not available")
+    if not os.path.exists(os.path.join(LIBDIR, "libpkb200.so")):
+        pytest.skip("libpkb200.so not built")
+    exe = tmp_path / "runtime_test"
+    cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-Werror",
+           "-I", os.path.join(ROOT, "include"), "-I", CUDA_INC,
+           os.path.join(ROOT, "tests", "cpp", "runtime_test.cpp"), "-o", str(exe),
+           "-L", LIBDIR, "-lpkb200", f"-Wl,-rpath,{LIBDIR}"]
+    if os.path.isdir(CUDA_LIB):
+        cmd += ["-L", CUDA_LIB, f"-Wl,-rpath,{CUDA_LIB}", f"-Wl,-rpath-link,{CUDA_LIB}"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    r = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "ALL PASSED" in r.stdout, r.stdout + r.stderr
