@@ -264,3 +264,83 @@ def autotune(op, M, N, K, iters=10, warmup=3, seed=0, inject_broken=False, repor
         return []
     t, _, cfg, m = min(valid, key=lambda r: r[0])
     return [entry(device_arch(), op, M, N, K, cfg, t, True, m)]
+
+
+# --------------------------------------------------------------------- CLI --
+def main(argv=None):
+    """python -m polykernel_b200.tuning <command> ...
+
+    enumerate [--limit N]        the pruned tcgen05 config space, one JSON object per line
+                                 (the reference driver's `enumerate --limit N`)
+    validate FILE...             schema-check cache files; exit 1 on the first error
+    show FILE                    one line per entry: gpu op MxNxK best validated time
+    autotune --op OP --shape M N K [--shape ...] --out FILE [--inject-broken]
+                                 tune on this GPU and merge the validated winners into FILE
+    """
+    import argparse
+    import json
+    import os
+    import sys
+    ap = argparse.ArgumentParser(prog="python -m polykernel_b200.tuning")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    p_en = sub.add_parser("enumerate")
+    p_en.add_argument("--limit", type=int, default=None)
+    p_va = sub.add_parser("validate")
+    p_va.add_argument("files", nargs="+")
+    p_sh = sub.add_parser("show")
+    p_sh.add_argument("file")
+    p_at = sub.add_parser("autotune")
+    p_at.add_argument("--op", required=True,
+                      choices=["matmul", "fused_matmul_bias_gelu", "matmul_bias_residual"])
+    p_at.add_argument("--shape", nargs=3, type=int, action="append", required=True,
+                      metavar=("M", "N", "K"))
+    p_at.add_argument("--out", required=True)
+    p_at.add_argument("--iters", type=int, default=10)
+    p_at.add_argument("--inject-broken", action="store_true",
+                      help="add a fast-but-wrong candidate; the gate must reject it")
+    a = ap.parse_args(argv)
+    if a.cmd == "enumerate":
+        for c in ConfigSpace.enumerate(a.limit):
+            print(json.dumps(c))
+        return 0
+    if a.cmd == "validate":
+        for f in a.files:
+            try:
+                n = len(load(f)["entries"])
+            except (OSError, ValueError) as e:
+                print(f"{f}: {e}", file=sys.stderr)
+                return 1
+            print(f"{f}: ok ({n} entries)")
+        return 0
+    if a.cmd == "show":
+        try:
+            doc = load(a.file)
+        except (OSError, ValueError) as e:
+            print(f"{a.file}: {e}", file=sys.stderr)
+            return 1
+        for e in doc["entries"]:
+            s, b = e["shape"], e["best"]
+            print(f"{e['gpu']} {e['op']} {s['M']}x{s['N']}x{s['K']} {s['dtype']} "
+                  f"block_n={b['block_n']} stages={b['shared_memory_stages']} "
+                  f"validated={e['validated']} time_ms={e['time_ms']}")
+        return 0
+    doc = load(a.out) if os.path.exists(a.out) else {"version": 1, "entries": []}
+    for M, N, K in a.shape:
+        report = []
+        found = autotune(a.op, M, N, K, iters=a.iters, inject_broken=a.inject_broken,
+                         report=report)
+        for r in report:
+            print(json.dumps({"op": a.op, "shape": [M, N, K], **{k: r[k] for k in
+                              ("label", "time_ms", "validated")}}))
+        if not found:
+            print(f"{a.op} {M}x{N}x{K}: no candidate passed the correctness gate",
+                  file=sys.stderr)
+            return 1
+        doc = merge(doc, found)
+    save(doc, a.out)
+    return 0
+
+
+if __name__ == "__main__":
+    import sys
+    sys.exit(main())

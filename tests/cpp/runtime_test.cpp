@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
+#include <iterator>
 #include <string>
 #include <vector>
 
@@ -217,8 +218,24 @@ static void test_library_launchers() {
   CHECK(!rt.Run("matmul", Shape{128, 128, 128}, nullptr, err) && contains(err, "no I/O bundle"));
 }
 
+// A cache written by the Python tuning module (polykernel_b200.tuning.save)
+// loads here unchanged: one schema, two writers.
+static void test_python_written_cache(const std::string& path) {
+  std::ifstream f(path);
+  CHECK(static_cast<bool>(f));
+  std::string text((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  KernelCache cache;
+  std::string err;
+  CHECK(cache.LoadTuningCache(text, err));
+  CHECK(cache.Size() == 2);
+  SelectionResult s = cache.Select("sm_100", "fused_matmul_bias_gelu", Shape{2048, 16384, 4096});
+  CHECK(s.ok() && s.entry->best.block_n == 128 && s.entry->best.shared_memory_stages == 6);
+  CHECK(!cache.Select("sm_100", "matmul", Shape{64, 64, 64}).ok());  // validated: false
+}
+
 int main(int argc, char** argv) {
   const std::string tmp = argc > 1 ? argv[1] : "/tmp";
+  if (argc > 2) test_python_written_cache(argv[2]);
   test_detect();
   test_selection_and_serve();
   test_unvalidated_and_missing_launcher();

@@ -26,5 +26,13 @@ def test_cpp_runtime(tmp_path):
         cmd += ["-L", CUDA_LIB, f"-Wl,-rpath,{CUDA_LIB}", f"-Wl,-rpath-link,{CUDA_LIB}"]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-3000:]
-    r = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=120)
+    from polykernel_b200 import tuning as T
+    corr = {"cosine": 1.0, "max_rel_err": 0.0, "pcc": 1.0}
+    doc = T.merge({"version": 1, "entries": []}, [
+        T.entry("sm_100", "fused_matmul_bias_gelu", 2048, 16384, 4096,
+                dict(T.DEFAULT, block_n=128, shared_memory_stages=6), 0.12, True, corr),
+        T.entry("sm_100", "matmul", 64, 64, 64, T.DEFAULT, None, False, corr)])
+    T.save(doc, tmp_path / "py_cache.json")
+    r = subprocess.run([str(exe), str(tmp_path), str(tmp_path / "py_cache.json")],
+                       capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and "ALL PASSED" in r.stdout, r.stdout + r.stderr

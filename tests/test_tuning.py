@@ -175,3 +175,28 @@ def test_autotune_rejects_injected_broken_variant(cuda):
     assert broken[0]["time_ms"] <= min(r["time_ms"] for r in report)
     assert len(entries) == 1 and entries[0]["validated"]
     assert (entries[0]["best"]["block_n"], entries[0]["best"]["shared_memory_stages"]) in T.COMPILED
+
+
+def test_cli_enumerate_validate_show(tmp_path, capsys):
+    import json as _json
+    assert T.main(["enumerate", "--limit", "2"]) == 0
+    lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.strip()]
+    assert len(lines) == 2
+    assert all((_json.loads(ln)["block_n"], _json.loads(ln)["shared_memory_stages"]) in T.COMPILED
+               for ln in lines)
+    doc = T.merge({"version": 1, "entries": []},
+                  [T.entry("sm_100", "matmul", 256, 512, 1024, T.DEFAULT, 0.01, True,
+                           {"cosine": 1.0, "max_rel_err": 0.0, "pcc": 1.0})])
+    good = tmp_path / "good.json"
+    T.save(doc, good)
+    assert T.main(["validate", str(good)]) == 0
+    assert "ok (1 entries)" in capsys.readouterr().out
+    assert T.main(["show", str(good)]) == 0
+    out = capsys.readouterr().out
+    assert "sm_100 matmul 256x512x1024 bf16 block_n=256 stages=4 validated=True" in out
+    bad = tmp_path / "bad.json"
+    d = _json.loads(good.read_text())
+    d["entries"][0]["validated"] = "yes"
+    bad.write_text(_json.dumps(d))
+    assert T.main(["validate", str(good), str(bad)]) == 1
+    assert "validated" in capsys.readouterr().err
