@@ -39,6 +39,11 @@ int pkb200_rmsnorm(const void* input, const void* weight, void* output, int rows
 /* Exact erf GELU over n elements. Replaces launch_gelu (gelu.cu:56). */
 int pkb200_gelu(const void* input, void* output, long long n, void* stream);
 
+/* Row softmax over the last axis, fp32 math, bf16 out (golden.py:75-80).
+ * Replaces launch_softmax (kernels/generated/softmax.cu), which the
+ * reference's cuda_run_main.cpp:64 declares. */
+int pkb200_softmax(const void* input, void* output, int rows, int cols, void* stream);
+
 /* C = bf16(A @ B); A [M,K], B [K,N]. Replaces launch_matmul (matmul.cu:78-79). */
 int pkb200_matmul(const void* A, const void* B, void* C, int M, int N, int K, void* stream);
 
@@ -308,6 +313,8 @@ int pkb200_path_counters(long long* out, int n);
 void launch_rmsnorm(const __nv_bfloat16* input, const __nv_bfloat16* weight,
                     __nv_bfloat16* output, int rows, int cols, float epsilon, void* stream);
 void launch_gelu(const __nv_bfloat16* input, __nv_bfloat16* output, int n, void* stream);
+void launch_softmax(const __nv_bfloat16* input, __nv_bfloat16* output, int rows, int cols,
+                    void* stream);
 void launch_matmul(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M,
                    int N, int K, void* stream);
 void launch_fused_rmsnorm_matmul(const __nv_bfloat16* input, const __nv_bfloat16* weight,

@@ -77,6 +77,13 @@ def gelu(x):
     return bf16((F32(0.5) * xf) * (F32(1.0) + e))
 
 
+def softmax(x):
+    """golden.softmax (golden.py:75-80): fp32 exp(x - max) / sum over the last axis."""
+    xf = bf16(x)
+    e = np.exp(xf - np.max(xf, axis=-1, keepdims=True))
+    return bf16(e / np.sum(e, axis=-1, keepdims=True))
+
+
 def rmsnorm(x, weight=None, eps=1e-5):
     """golden.rmsnorm (golden.py:83-90): x / sqrt(mean(x^2)+eps) [* w], fp32."""
     xf = bf16(x)

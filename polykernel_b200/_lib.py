@@ -19,6 +19,7 @@ SIGNATURES = {
     "pkb200_version": (ctypes.c_char_p, []),
     "pkb200_rmsnorm": (c_int, [_P, _P, _P, c_int, c_int, c_float, _P]),
     "pkb200_gelu": (c_int, [_P, _P, c_longlong, _P]),
+    "pkb200_softmax": (c_int, [_P, _P, c_int, c_int, _P]),
     "pkb200_matmul": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_matmul_f32out": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
     "pkb200_fused_rmsnorm_matmul": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P]),

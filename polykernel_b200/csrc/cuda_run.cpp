@@ -222,6 +222,30 @@ int run_gelu(int argc, char** argv) {
   return st;
 }
 
+// softmax IN OUT [--axis A]: last axis only (the reference's cuda_run_main.cpp:210-234).
+int run_softmax(int argc, char** argv) {
+  const char* u = "softmax IN OUT [--axis A]";
+  if (argc < 4) return usage(u);
+  int axis = -1;
+  for (int i = 4; i < argc; ++i) {
+    const std::string a = argv[i];
+    if (a == "--axis" && i + 1 < argc)
+      axis = std::atoi(argv[++i]);
+    else
+      return usage(u);
+  }
+  Npy in = read_npy(argv[2], "<V2");
+  if (in.shape.empty() || (axis != -1 && axis != static_cast<int>(in.shape.size()) - 1)) {
+    std::fprintf(stderr, "softmax: only last-axis reduction supported (axis=-1)\n");
+    return 1;
+  }
+  const int64_t cols = in.shape.back(), rows = cols ? in.size() / cols : 0;
+  Dev din(in), dout(in.bytes.size());
+  int st = finish(pkb200_softmax(din.p, dout.p, (int)rows, (int)cols, nullptr), "softmax");
+  if (!st) download(dout, in.shape, argv[3]);
+  return st;
+}
+
 int run_matmul(int argc, char** argv) {
   if (argc != 5) return usage("matmul A B C");
   Npy a = read_npy(argv[2], "<V2"), b = read_npy(argv[3], "<V2");
@@ -424,6 +448,7 @@ int main(int argc, char** argv) {
     if (op == "rmsnorm") return run_rmsnorm(argc, argv);
     if (op == "gelu") return run_gelu(argc, argv);
     if (op == "matmul") return run_matmul(argc, argv);
+    if (op == "softmax") return run_softmax(argc, argv);
     if (op == "fused_rmsnorm_matmul") return run_fused_rmsnorm_matmul(argc, argv);
     if (op == "fused_matmul_bias_gelu") return run_fused_matmul_bias_gelu(argc, argv);
     if (op == "matmul_int8") return run_matmul_int8(argc, argv);

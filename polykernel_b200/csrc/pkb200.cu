@@ -809,6 +809,18 @@ int pkb200_rmsnorm(const void* input, const void* weight, void* output, int rows
   return run_rmsnorm(cb(input), cb(weight), b(output), rows, cols, eps, S(stream));
 }
 
+int pkb200_softmax(const void* input, void* output, int rows, int cols, void* stream) {
+  if (rows < 0 || cols < 0) return cudaErrorInvalidValue;
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  if (!input || !output) return cudaErrorInvalidValue;
+  const int rows_per_block = 8;
+  const long long blocks = (static_cast<long long>(rows) + rows_per_block - 1) / rows_per_block;
+  softmax_rows_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, S(stream)>>>(
+      cb(input), b(output), rows, cols);
+  g_counters[kCntOther]++;
+  return cudaGetLastError();
+}
+
 int pkb200_gelu(const void* input, void* output, long long n, void* stream) {
   if (n < 0) return cudaErrorInvalidValue;
   if (n == 0) return cudaSuccess;
@@ -1531,6 +1543,9 @@ void launch_rmsnorm(const bf16* input, const bf16* weight, bf16* output, int row
 }
 void launch_gelu(const bf16* input, bf16* output, int n, void* stream) {
   report("launch_gelu", pkb200_gelu(input, output, n, stream));
+}
+void launch_softmax(const bf16* input, bf16* output, int rows, int cols, void* stream) {
+  report("launch_softmax", pkb200_softmax(input, output, rows, cols, stream));
 }
 void launch_matmul(const bf16* A, const bf16* B, bf16* C, int M, int N, int K, void* stream) {
   report("launch_matmul", pkb200_matmul(A, B, C, M, N, K, stream));

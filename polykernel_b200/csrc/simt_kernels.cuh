@@ -22,6 +22,27 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Row softmax (golden.py:75-80; the reference's kernels/generated/softmax.cu):
+// m = max(x), e = exp(x - m), y = bf16(e / sum(e)), all in fp32. One warp per
+// row, three passes over the row (max, sum, normalise); the row stays in L1/L2
+// between passes. Rows of -inf only produce NaN, as the golden does.
+__global__ void softmax_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                    __nv_bfloat16* __restrict__ out, long long rows, int cols) {
+  const long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat16* xr = x + r * cols;
+  __nv_bfloat16* yr = out + r * cols;
+  float m = -INFINITY;
+  for (int c = lane; c < cols; c += 32) m = fmaxf(m, __bfloat162float(xr[c]));
+  m = warp_max(m);
+  float sum = 0.f;
+  for (int c = lane; c < cols; c += 32) sum += expf(__bfloat162float(xr[c]) - m);
+  sum = warp_sum(sum);
+  for (int c = lane; c < cols; c += 32)
+    yr[c] = __float2bfloat16_rn(expf(__bfloat162float(xr[c]) - m) / sum);
+}
+
 // ------------------------------------------------------------------ RMSNorm --
 // out[r, :] = bf16((x / sqrt(mean(x^2) + eps)) * w)   (golden.py:83-90,
 // cpu_reference.cpp:16-44). One warp per row; the division is the correctly

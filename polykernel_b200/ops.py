@@ -61,6 +61,16 @@ def gelu(x):
     return y
 
 
+def softmax(x):
+    """golden.softmax over the last axis (launch_softmax, softmax.cu)."""
+    _req(x, "x")
+    cols = x.shape[-1] if x.dim() else 1
+    rows = x.numel() // max(cols, 1)
+    y = torch.empty_like(x)
+    check(lib().pkb200_softmax(_ptr(x), _ptr(y), rows, cols, _stream()), "softmax")
+    return y
+
+
 def _mk(a, b):
     _req(a, "a")
     _req(b, "b", dims=2)

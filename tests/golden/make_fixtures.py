@@ -169,6 +169,13 @@ def main():
         f8[f"{fmt}_edge_in"] = bits(e)
         f8[f"{fmt}_edge_code"] = e.astype(dt).view(np.uint8)
     np.savez_compressed(os.path.join(HERE, "golden_fp8.npz"), **f8)
+    # -------------------------------------------------- softmax (cuda_run op)
+    sm = {}
+    for name, shape in (("tokens_vocab", (64, 256)), ("odd", (32, 127)),  # test_cuda_run.py:366-378
+                        ("flat3d", (2, 16, 64)), ("long", (4, 5000))):
+        x = uni(shape) if name != "long" else (4 * rng.standard_normal(shape)).astype(np.float32).astype(BF)
+        sm[f"{name}_x"], sm[f"{name}_y"] = bits(x), bits(G.softmax(x))
+    np.savez_compressed(os.path.join(HERE, "golden_softmax.npz"), **sm)
     print("fixtures written to", HERE)
 
 

@@ -122,3 +122,17 @@ def test_fp8sim_through_harness(golden, cuda, tmp_path, fmt):
 
 def test_fp8sim_usage():
     assert _run("fp8sim", "e3m4", "a.npy", "w.npy", "c.npy").returncode == 2
+
+
+@pytest.mark.gpu
+def test_softmax_through_harness(golden, cuda, tmp_path):
+    """`softmax IN OUT [--axis A]` with the reference's arguments (last axis only)."""
+    g = golden("softmax")
+    _save(tmp_path / "x.npy", g["flat3d_x"])
+    assert _run("softmax", tmp_path / "x.npy", tmp_path / "y.npy").returncode == 0
+    check_gate(F(_load(tmp_path / "y.npy")), F(g["flat3d_y"]), min_exact=0.97)
+    assert _run("softmax", tmp_path / "x.npy", tmp_path / "y.npy", "--axis", "0").returncode == 1
+
+
+def test_softmax_usage():
+    assert _run("softmax", "only_in.npy").returncode == 2

@@ -222,3 +222,17 @@ def test_qkv_projection_feeds_attention(golden, pk):
     o = pk.ops.attention_prefill(q, k, v, causal=True)       # the layout attention consumes
     check_attention(f32_from_t(o), O.attention_prefill(f32_from_t(q), f32_from_t(k), f32_from_t(v)))
     assert Kd == 256
+
+
+# ---------------------------------------------------------------- softmax ----
+@pytest.mark.parametrize("name", ["tokens_vocab", "odd", "flat3d", "long"])
+def test_softmax_vs_golden(golden, pk, name):
+    """launch_softmax (the op the reference's cuda_run_main.cpp:64 declares)
+    against the golden's softmax fixtures (test_cuda_run.py:366-378 shapes plus
+    a long row): CUDA expf vs NumPy exp and the sum order differ by a few fp32
+    ulps, so a few bf16 outputs may sit one ulp away."""
+    g = golden("softmax")
+    x = t_from_bits(g[f"{name}_x"])
+    y = pk.ops.softmax(x)
+    assert tuple(y.shape) == tuple(x.shape)
+    check_gate(f32_from_t(y), F(g[f"{name}_y"]), min_exact=0.97)

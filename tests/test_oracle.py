@@ -233,3 +233,9 @@ def test_reference_cpu_fp8_rounding_matches_oracle(tmp_path, fmt):
     c = F(np.load(tmp_path / "c.npy").view(np.uint16))
     # compared as values: the driver's fp32 sum turns fp8(-0) into +0
     assert np.array_equal(c, O.fp8_round(w, fmt))
+
+
+@pytest.mark.parametrize("name", ["tokens_vocab", "odd", "flat3d", "long"])
+def test_softmax_bit_exact(golden, name):
+    g = golden("softmax")
+    assert np.array_equal(O.to_bits(O.softmax(F(g[f"{name}_x"]))), g[f"{name}_y"])
