@@ -148,6 +148,9 @@ int pkb200_ipc_alloc(size_t bytes, void** ptr, void* handle64);
 int pkb200_ipc_open(const void* handle64, void** ptr);
 int pkb200_ipc_close(void* ptr);
 int pkb200_free(void* ptr);
+/* One copy-engine copy in stream order (cudaMemcpyAsync, direction inferred
+ * from the pointers; a peer pointer from pkb200_ipc_open is fine). */
+int pkb200_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_peer_streams,
                         float* y32, float* const* slots, void* const* rows,
                         unsigned int* const* flags, unsigned int* epoch_src, void** plan_out);

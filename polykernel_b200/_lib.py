@@ -40,6 +40,7 @@ SIGNATURES = {
     "pkb200_ipc_open": (c_int, [_P, _P]),
     "pkb200_ipc_close": (c_int, [_P]),
     "pkb200_free": (c_int, [_P]),
+    "pkb200_copy_async": (c_int, [_P, _P, c_size_t, _P]),
     "pkb200_tp_ce_create": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P,
                                     _P]),
     "pkb200_tp_ce_destroy": (c_int, [_P]),

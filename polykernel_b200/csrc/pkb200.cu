@@ -942,6 +942,12 @@ int pkb200_ipc_close(void* ptr) { return ptr ? cudaIpcCloseMemHandle(ptr) : cuda
 
 int pkb200_free(void* ptr) { return ptr ? cudaFree(ptr) : cudaSuccess; }
 
+int pkb200_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return cudaSuccess;
+  if (!dst || !src) return cudaErrorInvalidValue;
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, S(stream));
+}
+
 int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_peer_streams,
                         float* y32, float* const* slots, void* const* rows, unsigned* const* flags,
                         unsigned* epoch_src, void** plan_out) {

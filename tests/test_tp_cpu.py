@@ -94,3 +94,12 @@ def test_shard_range_rejects_uneven():
     assert shard_range(28672, 3, 8) == (10752, 14336)
     with pytest.raises(ValueError):
         shard_range(10, 0, 3)
+
+
+def test_tp_bench_cli_help():
+    """The TP exchange benchmark's command line parses without a GPU."""
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, "-m", "polykernel_b200.tp_bench", "--help"],
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "--chunks" in r.stdout
