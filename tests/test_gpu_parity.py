@@ -236,3 +236,37 @@ def test_softmax_vs_golden(golden, pk, name):
     y = pk.ops.softmax(x)
     assert tuple(y.shape) == tuple(x.shape)
     check_gate(f32_from_t(y), F(g[f"{name}_y"]), min_exact=0.97)
+
+
+# ------------------------------------------------- fused == unfused, negatives ----
+@pytest.mark.parametrize("name", ["sq", "odd", "tiles"])
+def test_device_fused_equals_unfused(golden, pk, name):
+    """On the device the fused entry points give the unfused chains' bits
+    (the reference's test_golden_self.py:91-124, here through the C ABI)."""
+    g = golden("gemm")
+    a, b, bias = (t_from_bits(g[f"{name}_{k}"]) for k in ("a", "b", "bias"))
+    assert np.array_equal(bits_from_t(pk.ops.fused_rmsnorm_matmul(a, b)),
+                          bits_from_t(pk.ops.matmul(pk.ops.rmsnorm(a), b)))
+    # bias + GELU: the epilogue and the standalone GELU kernel share one GELU
+    # routine; the bias add rounds to bf16 in both (torch's bf16 add rounds
+    # the fp32 sum to nearest even, as golden.bias does)
+    unfused = pk.ops.gelu((pk.ops.matmul(a, b) + bias).contiguous())
+    fused = pk.ops.fused_matmul_bias_gelu(a, b, bias)
+    exact = float(np.mean(bits_from_t(fused) == bits_from_t(unfused)))
+    assert exact >= 0.999, exact
+    check_gate(f32_from_t(fused), f32_from_t(unfused), min_exact=0.999)
+
+
+def test_device_gate_rejects_transposed_operand_and_corruption(golden, pk):
+    """A GEMM fed the transposed B (the reference's mma_bad) and a corrupted
+    output (--corrupt) fail the gate the passing kernel meets."""
+    g = golden("gemm")
+    a, b = t_from_bits(g["sq_a"]), t_from_bits(g["sq_b"])
+    ref = F(g["sq_mm"])
+    good = f32_from_t(pk.ops.matmul(a, b))
+    check_parity(good, ref)
+    bad = f32_from_t(pk.ops.matmul(a, b.t().contiguous()))
+    with pytest.raises(AssertionError):
+        check_parity(bad, ref)
+    with pytest.raises(AssertionError):
+        check_parity(O.bf16(good * 1.5), ref)

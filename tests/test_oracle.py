@@ -239,3 +239,30 @@ def test_reference_cpu_fp8_rounding_matches_oracle(tmp_path, fmt):
 def test_softmax_bit_exact(golden, name):
     g = golden("softmax")
     assert np.array_equal(O.to_bits(O.softmax(F(g[f"{name}_x"]))), g[f"{name}_y"])
+
+
+@pytest.mark.parametrize("name", ["sq", "odd", "tiles"])
+def test_fused_equals_unfused_bit_exact(golden, name):
+    """The fused ops are the unfused chains with the same rounding points
+    (the reference's test_golden_self.py:91-124)."""
+    g = golden("gemm")
+    a, b, bias = F(g[f"{name}_a"]), F(g[f"{name}_b"]), F(g[f"{name}_bias"])
+    assert np.array_equal(O.to_bits(O.fused_rmsnorm_matmul(a, b)),
+                          O.to_bits(O.matmul(O.rmsnorm(a), b)))
+    assert np.array_equal(O.to_bits(O.fused_matmul_bias_gelu(a, b, bias)),
+                          O.to_bits(O.gelu(O.bias(O.matmul(a, b), bias))))
+
+
+def test_gate_rejects_transposed_operand_and_corruption(golden):
+    """Negative pins on the CPU oracle: a transposed B (the reference's mma_bad,
+    test_mma.py:288-328) and a scaled output (--corrupt, test_mlp_correctness.py:
+    199-208) both fail the gate the GPU tests apply."""
+    from tests.helpers import check_parity
+    g = golden("gemm")
+    a, b = F(g["sq_a"]), F(g["sq_b"])
+    ref = F(g["sq_mm"])
+    with pytest.raises(AssertionError):
+        check_parity(O.matmul(a, np.ascontiguousarray(b.T)), ref)
+    with pytest.raises(AssertionError):
+        check_parity(O.bf16(ref * 1.5), ref)
+    check_parity(O.matmul(a, b), ref)
