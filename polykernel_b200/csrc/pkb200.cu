@@ -1139,6 +1139,8 @@ int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void
 }
 
 int pkb200_quantize_fp8(const void* W, uint8_t* Wf8, long long n, int fmt, void* stream) {
+  if (fmt != kFp8E4M3 && fmt != kFp8E5M2) return cudaErrorInvalidValue;
+  if (n <= 0) return n < 0 ? cudaErrorInvalidValue : cudaSuccess;
   DeviceInfo* di = nullptr;
   int e = current_device_info(&di);
   if (e) return e;
@@ -1146,6 +1148,8 @@ int pkb200_quantize_fp8(const void* W, uint8_t* Wf8, long long n, int fmt, void*
 }
 
 int pkb200_dequantize_fp8(const uint8_t* Wf8, void* W, long long n, int fmt, void* stream) {
+  if (fmt != kFp8E4M3 && fmt != kFp8E5M2) return cudaErrorInvalidValue;
+  if (n <= 0) return n < 0 ? cudaErrorInvalidValue : cudaSuccess;
   DeviceInfo* di = nullptr;
   int e = current_device_info(&di);
   if (e) return e;

@@ -80,3 +80,37 @@ def test_ops_reject_cpu_tensors():
         ops.gelu(x)
     with pytest.raises(ValueError):
         ops.matmul(x, torch.zeros(8, 8, dtype=torch.bfloat16))
+
+
+def test_empty_and_negative_sizes_without_a_device():
+    """Empty inputs are no-ops and negative sizes are cudaErrorInvalidValue (1),
+    decided before any device work, so this runs without a GPU (the reference's
+    launchers likewise return before launching for empty shapes)."""
+    import ctypes
+    from polykernel_b200 import _lib
+    L = _lib.lib()
+    P = None
+    eps = ctypes.c_float(1e-5)
+    zero = [L.pkb200_matmul(P, P, P, 0, 8, 8, P),
+            L.pkb200_matmul(P, P, P, 8, 0, 8, P),
+            L.pkb200_fused_matmul_bias_gelu(P, P, P, P, 0, 8, 8, P),
+            L.pkb200_fused_rmsnorm_matmul(P, P, P, P, 0, 8, 8, eps, P),
+            L.pkb200_rmsnorm(P, P, P, 0, 8, eps, P),
+            L.pkb200_gelu(P, P, 0, P),
+            L.pkb200_softmax(P, P, 0, 8, P),
+            L.pkb200_softmax(P, P, 4, 0, P),
+            L.pkb200_attention_prefill(P, P, P, P, 1, 1, 0, 0, 64, ctypes.c_float(0.125), 1, P),
+            L.pkb200_kv_cache_update(P, P, P, 1, 1, 0, 0, 64, P),
+            L.pkb200_matmul_int8(P, P, P, P, 0, 8, 8, P),
+            L.pkb200_mlp_block(P, P, P, P, P, P, P, 0, 8, 8, ctypes.c_float(1e-6), P, 0, P),
+            L.pkb200_matmul_fp8_sim(P, P, P, 0, 8, 8, 0, P),
+            L.pkb200_quantize_fp8(P, P, 0, 0, P),
+            L.pkb200_dequantize_fp8(P, P, 0, 1, P)]
+    assert zero == [0] * len(zero)
+    negative = [L.pkb200_matmul(P, P, P, -1, 8, 8, P),
+                L.pkb200_softmax(P, P, -1, 8, P),
+                L.pkb200_rmsnorm(P, P, P, -1, 8, eps, P),
+                L.pkb200_quantize_fp8(P, P, -4, 0, P),
+                L.pkb200_matmul_fp8_sim(P, P, P, 0, 8, 8, 5, P),   # unknown fp8 format
+                L.pkb200_quantize_fp8(P, P, 0, 7, P)]
+    assert negative == [1] * len(negative)
