@@ -36,3 +36,29 @@ def test_cpp_runtime(tmp_path):
     r = subprocess.run([str(exe), str(tmp_path), str(tmp_path / "py_cache.json")],
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and "ALL PASSED" in r.stdout, r.stdout + r.stderr
+
+
+def test_cpp_runtime_real_detectors(tmp_path):
+    """CudaDeviceDetector (built with PKB200_RUNTIME_CUDA) and the library-backed
+    detector agree: "sm_100" on a B200, a typed detection failure without one."""
+    if shutil.which("g++") is None or not os.path.isdir(CUDA_LIB):
+        pytest.skip("g++ or the CUDA runtime library not available")
+    if not os.path.exists(os.path.join(LIBDIR, "libpkb200.so")):
+        pytest.skip("libpkb200.so not built")
+    exe = tmp_path / "detect_probe"
+    cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-Werror", "-DPKB200_RUNTIME_CUDA",
+           "-I", os.path.join(ROOT, "include"), "-I", CUDA_INC,
+           os.path.join(ROOT, "tests", "cpp", "detect_probe.cpp"), "-o", str(exe),
+           "-L", LIBDIR, "-lpkb200", f"-Wl,-rpath,{LIBDIR}",
+           "-L", CUDA_LIB, "-lcudart", f"-Wl,-rpath,{CUDA_LIB}"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    import torch
+    if torch.cuda.is_available():
+        assert "cuda=sm_100 library=sm_100" in r.stdout
+        assert "no tuned kernel for sm_100/matmul/M=8,N=8,K=8,bf16" in r.stdout
+    else:
+        assert "cuda=none library=none" in r.stdout
+        assert "device detection failed" in r.stdout
