@@ -301,6 +301,13 @@ int polykernel_fused_mlp_block(float* in, float* out, int M, int N, int K);
  * tensor-core kernels set on timeout (0 = none). Synchronises the device. */
 int pkb200_device_error(int* code);
 
+/* Number of tensor-core attention CTAs, since load on the current device, that
+ * recomputed their query rows with the exact fp32 row routine because a V
+ * tile held values the fp16 P.V pass cannot carry exactly (|v| >= 2^16,
+ * inf/NaN, or a tile of values all below 2^-6 with some below 2^-17).
+ * Synchronises the device. */
+int pkb200_attention_exact_ctas(unsigned long long* count);
+
 /* Counters of which implementation each entry point took since load:
  * out[0] tcgen05 GEMM launches, out[1] SIMT GEMM launches,
  * out[2] tcgen05 attention launches, out[3] SIMT attention launches,

@@ -205,27 +205,29 @@ def matmul_fp8_sim(a, w, fmt, acc=F32):
 
 
 # ----------------------------------------------------------------- attention --
-def attention_prefill(q, k, v, causal=True, scale=None):
+def attention_prefill(q, k, v, causal=True, scale=None, acc=F32):
     """Prefill SDPA (kernels/cpu/attention.cpp:95-163; golden.py:139-172):
     scores = q.k * scale in fp32 (scale defaults to 1/sqrt(D)), query row i sees
     key j <= S_kv - S_q + i when causal, softmax in fp32, P.V in fp32, one bf16
-    rounding. A row that sees no key yields 0."""
+    rounding. A row that sees no key yields 0. With acc=np.float64 every
+    intermediate is fp64 (same single bf16 rounding of O): the fp64-accumulated
+    reference that separates reduction-order noise from real error."""
     qf, kf, vf = bf16(q), bf16(k), bf16(v)
     D = qf.shape[-1]
     Sq, Skv = qf.shape[-2], kf.shape[-2]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    s = np.matmul(qf, np.swapaxes(kf, -1, -2)).astype(F32) * F32(scale)
+    s = np.matmul(qf.astype(acc), np.swapaxes(kf, -1, -2).astype(acc)).astype(acc) * acc(scale)
     if causal:
         i = np.arange(Sq)[:, None]
         j = np.arange(Skv)[None, :]
-        s = np.where(j <= (Skv - Sq + i), s, -np.inf).astype(F32)
-    m = np.max(s, axis=-1, keepdims=True)
-    m = np.where(np.isfinite(m), m, F32(0))
-    e = np.exp(s - m).astype(F32)
-    l = np.sum(e, axis=-1, keepdims=True, dtype=F32)
-    o = np.matmul(e, vf).astype(F32)
-    o = np.where(l > 0, o / np.where(l > 0, l, F32(1)), F32(0))
+        s = np.where(j <= (Skv - Sq + i), s, -np.inf).astype(acc)
+    m = np.max(s, axis=-1, keepdims=True) if Skv else np.zeros(s.shape[:-1] + (1,), acc)
+    m = np.where(np.isfinite(m), m, acc(0))
+    e = np.exp(s - m).astype(acc)
+    l = np.sum(e, axis=-1, keepdims=True, dtype=acc)
+    o = np.matmul(e, vf.astype(acc)).astype(acc)
+    o = np.where(l > 0, o / np.where(l > 0, l, acc(1)), acc(0))
     return bf16(o)
 
 

@@ -72,6 +72,7 @@ SIGNATURES = {
     "polykernel_fused_mlp_block": (c_int, [_P, _P, c_int, c_int, c_int]),
     "pkb200_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_path_counters": (c_int, [ctypes.POINTER(c_longlong), c_int]),
+    "pkb200_attention_exact_ctas": (c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
 }
 
 _lib = None
@@ -110,4 +111,12 @@ def path_counters() -> dict:
 def device_error() -> int:
     v = c_int(0)
     check(lib().pkb200_device_error(ctypes.byref(v)), "pkb200_device_error")
+    return int(v.value)
+
+
+def attention_exact_ctas() -> int:
+    """CTAs of the tensor-core attention kernel that took the exact fp32 row
+    path (V values outside the fp16 P.V pass's exact range), since load."""
+    v = ctypes.c_ulonglong(0)
+    check(lib().pkb200_attention_exact_ctas(ctypes.byref(v)), "pkb200_attention_exact_ctas")
     return int(v.value)

@@ -7,27 +7,53 @@
 // causal (attention_prefill.cu:103), softmax in fp32, P.V accumulated in fp32,
 // one bf16 rounding of O. Rows that see no key produce 0 (attention_prefill.cu:154).
 //
-// One CTA per (pair of 128-query tiles A and B, batch*head). Roles (320 threads):
-//   warps 0-3  softmax for tile A, warps 4-7 softmax for tile B. Thread r of a
-//              group owns query row r (= TMEM lane r). It reads its S row with
-//              tcgen05.ld, keeps the running max/sum in the exp2 domain, and
-//              writes P (bf16 pairs) back into the same TMEM columns with
-//              tcgen05.st, where the P.V MMA reads it as its A operand. O is
-//              rescaled in TMEM only when the row max grew by more than 2^8
-//              (exact: every P and the final sum use the same stale max). At
-//              the end the group normalises O and stores it.
-//   warp 8     TMA producer: Q tiles once; K and V tiles (128 keys) through two
-//              2-deep rings shared by both query tiles. For the append entry
-//              point, the CTA whose query tiles match a tile of new rows also
-//              writes those K/V tiles from shared memory into the cache with
-//              TMA stores, so the append costs no extra HBM read.
-//   warp 9     TMEM owner + single-thread MMA issuer. Order per key tile j:
-//              PV_A(j); S_A(j+1); PV_B(j); S_B(j+1). S_X(j+1) overwrites the TMEM
-//              columns that held P_X(j), so the issuer waits for PV_X(j) to
-//              complete first (PV_B(j) is queued meanwhile, keeping the tensor
-//              pipe busy). The two groups interleave: while one waits for its
-//              MMAs the other runs its exponentials.
-// TMEM (512 columns): S/P_A [0,128), S/P_B [128,256), O_A [256,256+D), O_B [384,384+D).
+// One CTA per (128-query tile, batch*head), longest tiles first. Roles (384
+// threads):
+//   warps 0-3  softmax. Thread r owns query row r (= TMEM lane r). It reads
+//              its S row with tcgen05.ld, keeps the running max/sum in the
+//              exp2 domain, and writes P back over the same TMEM columns as an
+//              fp16 pair per probability (P = P_hi + P_lo, ~22 significant
+//              bits), where the P.V MMAs read it as their A operand. Per key
+//              tile it hands the row's rescale factor (2^(m_old - m_new)) to
+//              the correction warps.
+//   warps 4-7  correction. Each key tile's P.V lands in a fresh TMEM
+//              accumulator Ot (16 MMA steps deep); thread r folds it into the
+//              running O of row r with fp32 FMAs, O = O * alpha + Ot, in TMEM.
+//              At the end it normalises O by the row sum and stores it.
+//   warp 8     TMA producer: the Q tile once; K and V tiles (128 keys) through
+//              2-deep rings. For the append entry point, the CTA whose query
+//              tile matches a tile of new rows also writes those K/V tiles
+//              from shared memory into the cache with TMA stores, so the
+//              append costs no extra HBM read.
+//   warp 9     TMEM owner + single-thread MMA issuer. Per key tile j: S(j+1)
+//              into the other S buffer (once P.V(j-1) has read it), then
+//              P.V(j) = P_hi.V + P_lo.V into Ot (once the correction warps have
+//              drained Ot). So the tensor core computes S(j+1) while the
+//              softmax works on S(j), and P.V(j) while the softmax works on
+//              S(j+1).
+//   warps 10-11 V converter: each V tile is rewritten in place in shared
+//              memory from bf16 to fp16 (same layout, same swizzle) before the
+//              P.V MMAs read it. Every bf16 value in [2^-17, 65280] is exactly
+//              an fp16 value. A tile that holds a value of magnitude >= 2^16
+//              (or inf), or a warp's share of a tile whose values are all
+//              below 2^-6 (where values below 2^-17 would lose bits), marks the
+//              CTA; such a CTA
+//              recomputes its query rows with the exact SIMT row routine after
+//              the tensor-core pass, so the result never depends on fp16 range.
+//
+// Numerics: scores are fp32 (bf16 Q.K on tensor cores), P is fp32 from the
+// SFU exp2 and enters P.V as fp16 hi+lo (relative error ~2^-22), V enters as
+// exact fp16, each key tile's P.V accumulates in fp32 on the tensor core over
+// only 128 keys, and the tiles are summed with round-to-nearest fp32 FMAs.
+// Tensor-core accumulation truncates; summing a 2048-key row in one tensor-core
+// accumulator would put its rounding well above the golden's fp32 sum, which
+// the per-tile accumulator avoids. This is the golden's arithmetic (fp32 P,
+// golden.py:139-172; attention_prefill.cu:127-147) to within fp32 summation
+// order.
+// TMEM (512 columns): S/P buffers [0,128) and [128,256), Ot [256,256+D),
+// O [384,384+D). Within an S/P buffer, the P of keys [64h, 64h+64) sits in
+// columns [64h, 64h+32) (hi) and [64h+32, 64h+64) (lo), one fp16 pair per
+// column.
 //
 // Key positions come from two sources (KvSources): A (rows [0, n_a), the
 // cache prefix or the whole K/V of the plain entry point) and B (the new
@@ -39,20 +65,27 @@
 
 namespace pkb200 {
 namespace attn {
-constexpr int BM = 128;       // query rows per tile (two tiles per CTA)
-constexpr int BN = 128;       // keys per tile
-constexpr int NUM_THREADS = 320;
+constexpr int BM = 128;           // query rows per tile (one tile per CTA)
+constexpr int BN = 128;           // keys per tile
+constexpr int KST = 2;            // K pipeline stages
+constexpr int VST = 3;            // V pipeline stages (TMA, then fp16 conversion)
+constexpr int NUM_THREADS = 384;
+constexpr int kConvThreads = 64;  // warps 10-11
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr uint32_t kColOt = 256;  // per-key-tile P.V accumulator
+constexpr uint32_t kColO = 384;   // running O
 
 template <int D>
 struct Layout {
-  static constexpr int DBOX = D / 64;                 // 64-column boxes per row
+  static constexpr int DBOX = D / 64;                   // 64-column boxes per row
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int OFF_Q = 0;                      // Q_A, Q_B
-  static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;    // 2 stages
-  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;   // 2 stages
-  static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;          // KST stages
+  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;   // VST stages
+  static constexpr int OFF_ALPHA = OFF_V + VST * KV_BYTES;  // float[2][BM]
+  static constexpr int OFF_L = OFF_ALPHA + 2 * BM * 4;     // float[BM]
+  static constexpr int OFF_BAR = OFF_L + BM * 4;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 };
 }  // namespace attn
@@ -68,10 +101,27 @@ struct AttnTcParams {
   int causal;
   int append;     // 1: write source-B tiles into the cache maps
   int num_qtiles;
-  int num_pairs;
   __nv_bfloat16* O;
   int* err;
+  // exact fallback (rows of CTAs whose V tiles fp16 cannot carry exactly)
+  const __nv_bfloat16* Q;
+  KvSources kv;
+  float scale;
+  unsigned long long* exact_ctas;  // count of CTAs that took the fallback
 };
+
+// Key tile j of query tile qt is a tile of new rows that this CTA appends.
+__device__ __forceinline__ bool attn_append_tile(const AttnTcParams& p, int j, int qt) {
+  return p.append && j >= p.tiles_a && j - p.tiles_a == qt;
+}
+
+// Rewrites one 32-bit word (two bf16) as two fp16 and folds |v| into amax
+// (one three-input max).
+__device__ __forceinline__ uint32_t attn_bf16x2_to_f16x2(uint32_t w, float& amax) {
+  const float f0 = __uint_as_float(w << 16), f1 = __uint_as_float(w & 0xffff0000u);
+  amax = fmax3(amax, fabsf(f0), fabsf(f1));
+  return pack_f16x2(f0, f1);
+}
 
 // Number of key tiles query tile `qt` visits (0 if the tile is past S_q).
 __device__ __forceinline__ int attn_tiles_for(const AttnTcParams& p, int qt) {
@@ -101,40 +151,58 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  float* alpha_s = reinterpret_cast<float*>(smem + L::OFF_ALPHA);
+  float* l_s = reinterpret_cast<float*>(smem + L::OFF_L);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* k_empty = bars + 3;   // [2]
-  uint64_t* v_full = bars + 5;    // [2]
-  uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [2]  per query tile (A, B)
-  uint64_t* p_full = bars + 11;   // [2]
-  uint64_t* pv_done = bars + 13;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* k_full = bars + 1;            // [KST]
+  uint64_t* k_empty = k_full + KST;       // [KST]
+  uint64_t* v_full = k_empty + KST;       // [VST] TMA landed (bf16)
+  uint64_t* v_empty = v_full + VST;       // [VST]
+  uint64_t* v_conv = v_empty + VST;       // [VST] converted to fp16
+  uint64_t* s_full = v_conv + VST;        // [2]  S(j) in S/P buffer j&1
+  uint64_t* p_full = s_full + 2;          // [2]  P(j) written over it
+  uint64_t* alpha_full = p_full + 2;      // [2]  rescale factors of tile j
+  uint64_t* alpha_empty = alpha_full + 2; // [2]
+  uint64_t* pv_done = alpha_empty + 2;    // P.V(j) in Ot
+  uint64_t* ot_free = pv_done + 1;        // Ot drained into O
+  uint64_t* l_ready = ot_free + 1;        // row sums in l_s
+  uint64_t* v_stored = l_ready + 1;       // appended V tile read out of smem
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_stored + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* needs_exact = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int bh = blockIdx.y;
-  const int pair = p.num_pairs - 1 - static_cast<int>(blockIdx.x);  // heavy pairs first
-  const int qt_a = 2 * pair, qt_b = 2 * pair + 1;
-  const int n_tile0 = attn_tiles_for(p, qt_a);
-  const int n_tile1 = attn_tiles_for(p, qt_b);
-  const int nmax = max(n_tile0, n_tile1);
-  const bool valid_b = qt_b * BM < p.S_q;
+  // One-dimensional grid ordered longest query tiles first across all heads,
+  // so the block scheduler fills the SMs longest-job-first.
+  const int bh = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.BH));
+  const int qt = p.num_qtiles - 1 - static_cast<int>(blockIdx.x / static_cast<unsigned>(p.BH));
+  const int nt = attn_tiles_for(p, qt);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VST; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&pv_done[i], 1);
+      mbar_init(&v_conv[i], kConvThreads);
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], BM);
+      mbar_init(&alpha_full[i], BM);
+      mbar_init(&alpha_empty[i], BM);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(ot_free, BM);
+    mbar_init(l_ready, BM);
+    mbar_init(v_stored, 1);
     *abort_flag = 0;
+    *needs_exact = 0;
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -147,171 +215,185 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    if (lane == 0 && nmax > 0) {
+    if (lane == 0 && nt > 0) {
       // -------------------------------------------------------- producer --
       tma_prefetch_desc(&map_q);
-      mbar_arrive_expect_tx(q_full, (valid_b ? 2 : 1) * L::Q_BYTES);
+      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
 #pragma unroll
-      for (int c = 0; c < L::DBOX; ++c) {
-        tma_load_3d(smem + L::OFF_Q + c * (BM * 128), &map_q, q_full, c * 64, qt_a * BM, bh);
-        if (valid_b)
-          tma_load_3d(smem + L::OFF_Q + L::Q_BYTES + c * (BM * 128), &map_q, q_full, c * 64,
-                      qt_b * BM, bh);
-      }
-      for (int j = 0; j < nmax; ++j) {
+      for (int c = 0; c < L::DBOX; ++c)
+        tma_load_3d(smem + L::OFF_Q + c * (BM * 128), &map_q, q_full, c * 64, qt * BM, bh);
+      for (int j = 0; j < nt; ++j) {
         const bool from_a = j < p.tiles_a;
         const int row0 = from_a ? j * BN : (j - p.tiles_a) * BN;
         const CUtensorMap* mk = from_a ? &map_ka : &map_kb;
         const CUtensorMap* mv = from_a ? &map_va : &map_vb;
-        const int new_tile = row0 / BN;
-        const bool do_append = p.append && !from_a && (new_tile == qt_a || new_tile == qt_b);
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        uint8_t* sk = smem + L::OFF_K + st * L::KV_BYTES;
-        uint8_t* sv = smem + L::OFF_V + st * L::KV_BYTES;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, p.err, abort_flag, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&k_full[st], L::KV_BYTES);
+        const int ks = j % KST, vs = j % VST;
+        const uint32_t kph = (j / KST) & 1, vph = (j / VST) & 1;
+        uint8_t* sk = smem + L::OFF_K + ks * L::KV_BYTES;
+        uint8_t* sv = smem + L::OFF_V + vs * L::KV_BYTES;
+        // V first: its conversion sits between the load and the P.V MMAs.
+        if (!mbar_wait(&v_empty[vs], vph ^ 1, p.err, abort_flag, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&v_full[vs], L::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < L::DBOX; ++c)
-          tma_load_3d(sk + c * (BN * 128), mk, &k_full[st], c * 64, row0, bh);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, p.err, abort_flag, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&v_full[st], L::KV_BYTES);
+          tma_load_3d(sv + c * (BN * 128), mv, &v_full[vs], c * 64, row0, bh);
+        if (!mbar_wait(&k_empty[ks], kph ^ 1, p.err, abort_flag, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&k_full[ks], L::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < L::DBOX; ++c)
-          tma_load_3d(sv + c * (BN * 128), mv, &v_full[st], c * 64, row0, bh);
-        if (do_append) {
-          // Write this tile of new rows into the cache (rows n_a + row0 ...).
-          if (!mbar_wait(&k_full[st], ph, p.err, abort_flag, kErrTimeoutProducer)) break;
+          tma_load_3d(sk + c * (BN * 128), mk, &k_full[ks], c * 64, row0, bh);
+        if (attn_append_tile(p, j, qt)) {
+          // Write this tile of new rows into the cache (rows n_a + row0 ...),
+          // V before the converter rewrites it as fp16.
+          if (!mbar_wait(&k_full[ks], kph, p.err, abort_flag, kErrTimeoutProducer)) break;
 #pragma unroll
           for (int c = 0; c < L::DBOX; ++c)
             tma_store_3d(&map_kc_store, sk + c * (BN * 128), c * 64, p.n_a + row0, bh);
-          if (!mbar_wait(&v_full[st], ph, p.err, abort_flag, kErrTimeoutProducer)) break;
+          if (!mbar_wait(&v_full[vs], vph, p.err, abort_flag, kErrTimeoutProducer)) break;
 #pragma unroll
           for (int c = 0; c < L::DBOX; ++c)
             tma_store_3d(&map_vc_store, sv + c * (BN * 128), c * 64, p.n_a + row0, bh);
           bulk_commit_group();
           bulk_wait_group_read0();
+          mbar_arrive(v_stored);
         }
       }
       bulk_wait_group0();
     }
   } else if (warp == 9) {
-    if (lane == 0 && nmax > 0) {
+    if (lane == 0 && nt > 0) {
       // ------------------------------------------------------ MMA issuer --
       constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
-      constexpr uint32_t idesc_o = make_idesc_bf16(BM, D, false, true);
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag, kErrTimeoutMma);
-      auto issue_s = [&](int x, int j) {
-        const uint32_t q_addr = smem_u32(smem + L::OFF_Q + x * L::Q_BYTES);
-        const uint32_t k_addr = smem_u32(smem + L::OFF_K + (j & 1) * L::KV_BYTES);
+      constexpr uint32_t idesc_o = make_idesc_f16(BM, D, false, true);
+      const uint32_t q_addr = smem_u32(smem + L::OFF_Q);
+      auto issue_s = [&](int j) {
+        const uint32_t k_addr = smem_u32(smem + L::OFF_K + (j % KST) * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint64_t ad = make_sw128_desc(q_addr + off, 16, 1024);
           const uint64_t bd = make_sw128_desc(k_addr + off, 16, 1024);
-          tc_mma_f16(tmem + x * BN, ad, bd, idesc_s, kk != 0);
+          tc_mma_f16(tmem + (j & 1) * BN, ad, bd, idesc_s, kk != 0);
         }
-        tc_commit(&s_full[x]);
+        tc_commit(&k_empty[j % KST]);
+        tc_commit(&s_full[j & 1]);
       };
-      auto issue_pv = [&](int x, int j) {
-        const uint32_t v_addr = smem_u32(smem + L::OFF_V + (j & 1) * L::KV_BYTES);
+      auto issue_pv = [&](int j) {
+        const uint32_t v_addr = smem_u32(smem + L::OFF_V + (j % VST) * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, BN * 128, 1024);
-          tc_mma_f16_tmem_a(tmem + 256 + x * 128, tmem + x * BN + kk * 8, bd, idesc_o,
-                            (j | kk) != 0);
+          const uint32_t a_hi = tmem + (j & 1) * BN + (kk >> 2) * 64 + (kk & 3) * 8;
+          tc_mma_f16_tmem_a(tmem + kColOt, a_hi, bd, idesc_o, kk != 0);
+          tc_mma_f16_tmem_a(tmem + kColOt, a_hi + 32, bd, idesc_o, 1);
         }
-        tc_commit(&pv_done[x]);
+        tc_commit(&v_empty[j % VST]);
+        tc_commit(pv_done);
       };
-      // prologue: S for key tile 0
+      bool ok = mbar_wait(q_full, 0, p.err, abort_flag, kErrTimeoutMma);
       if (ok) ok = mbar_wait(&k_full[0], 0, p.err, abort_flag, kErrTimeoutMma);
       if (ok) {
         tc_fence_after();
-        if (n_tile0 > 0) issue_s(0, 0);
-        if (n_tile1 > 0) issue_s(1, 0);
-        tc_commit(&k_empty[0]);
+        issue_s(0);
       }
-      for (int j = 0; j < nmax && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int jn = j + 1;
-        bool v_ready = false, k_next_ready = false;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const int nt = x == 0 ? n_tile0 : n_tile1;
-          if (!ok || j >= nt) continue;
-          if (!v_ready) {
-            ok = mbar_wait(&v_full[st], ph, p.err, abort_flag, kErrTimeoutMma);
-            v_ready = true;
-          }
-          if (ok) ok = mbar_wait(&p_full[x], j & 1, p.err, abort_flag, kErrTimeoutMma);
+      for (int j = 0; j < nt && ok; ++j) {
+        if (j + 1 < nt) {
+          // S(j+1) goes into the buffer that held P(j-1): P.V(j-1) must be done.
+          ok = mbar_wait(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1, p.err, abort_flag,
+                         kErrTimeoutMma);
+          if (ok && j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1, p.err, abort_flag, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(x, j);
-          if (jn < nt) {
-            if (!k_next_ready) {
-              ok = mbar_wait(&k_full[jn & 1], (jn >> 1) & 1, p.err, abort_flag, kErrTimeoutMma);
-              k_next_ready = true;
-            }
-            // S_X(j+1) reuses the TMEM columns P_X(j) occupies: wait for PV_X(j).
-            if (ok) ok = mbar_wait(&pv_done[x], j & 1, p.err, abort_flag, kErrTimeoutMma);
-            if (!ok) break;
-            tc_fence_after();
-            issue_s(x, jn);
-          }
+          issue_s(j + 1);
         }
+        ok = mbar_wait(&v_conv[j % VST], (j / VST) & 1, p.err, abort_flag, kErrTimeoutMma);
+        if (ok) ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, abort_flag, kErrTimeoutMma);
+        if (ok && j >= 1) ok = mbar_wait(ot_free, (j - 1) & 1, p.err, abort_flag, kErrTimeoutMma);
         if (!ok) break;
-        tc_commit(&v_empty[st]);
-        if (k_next_ready) tc_commit(&k_empty[jn & 1]);
+        tc_fence_after();
+        issue_pv(j);
       }
     }
-  } else {
+  } else if (warp >= 10) {
+    // ------------------------------------------------------ V converter --
+    const int t = static_cast<int>(threadIdx.x) - 320;
+    int appended = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int st = j % VST;
+      const uint32_t ph = (j / VST) & 1;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], ph, p.err, abort_flag,
+                                                  kErrTimeoutConvert));
+      if (ok && attn_append_tile(p, j, qt)) {
+        ok = __all_sync(0xffffffffu, mbar_wait(v_stored, appended & 1, p.err, abort_flag,
+                                               kErrTimeoutConvert));
+        ++appended;
+      }
+      if (!ok) break;
+      uint4* tile = reinterpret_cast<uint4*>(smem + L::OFF_V + st * L::KV_BYTES);
+      float amax = 0.f;
+#pragma unroll 8
+      for (int i = t; i < L::KV_BYTES / 16; i += kConvThreads) {
+        uint4 w = tile[i];
+        w.x = attn_bf16x2_to_f16x2(w.x, amax);
+        w.y = attn_bf16x2_to_f16x2(w.y, amax);
+        w.z = attn_bf16x2_to_f16x2(w.z, amax);
+        w.w = attn_bf16x2_to_f16x2(w.w, amax);
+        tile[i] = w;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&v_conv[st]);
+      // Range check per warp share of the tile: a value of magnitude >= 2^16
+      // (inf included), or a share whose largest magnitude is below 2^-6,
+      // where values below 2^-17 would lose bits in fp16. (A NaN in V
+      // propagates to O as it does in fp32.)
+      const float wmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+      if (lane == 0 && (!(wmax < 65536.f) || (wmax != 0.f && wmax < 0.015625f))) *needs_exact = 1;
+    }
+  } else if (warp < 4) {
     // ----------------------------------------------------------- softmax --
-    const int x = warp >> 2;        // query tile A (0) or B (1)
-    const int qw = warp & 3;        // TMEM lane quarter
-    const int r = qw * 32 + lane;   // query row within the tile == TMEM lane
-    const int qt = x == 0 ? qt_a : qt_b;
+    const int r = static_cast<int>(threadIdx.x);  // query row within the tile == TMEM lane
     const int qi = qt * BM + r;
-    const int ntiles = x == 0 ? n_tile0 : n_tile1;
     const int S_kv = p.n_a + p.n_b;
     const int limit = p.causal ? (S_kv - p.S_q + qi) : (S_kv - 1);
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(qw * 32) << 16);
-    const uint32_t s_col = x * BN;
-    const uint32_t o_col = 256 + x * 128;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float m_run = -INFINITY;
     float l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
+    for (int j = 0; j < nt; ++j) {
+      const int b = j & 1;
       const bool from_a = j < p.tiles_a;
       const int p0 = from_a ? j * BN : p.n_a + (j - p.tiles_a) * BN;
       const int cnt = from_a ? min(BN, p.n_a - j * BN) : min(BN, p.n_b - (j - p.tiles_a) * BN);
       const int nvalid = max(0, min(cnt, limit - p0 + 1));
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, p.err, abort_flag,
-                                             kErrTimeoutSoftmax));
-      if (!ok) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, p.err, abort_flag,
+                                             kErrTimeoutSoftmax)))
+        break;
       tc_fence_after();
       const bool full = __all_sync(0xffffffffu, nvalid == BN);
+      const float m_prev = m_run;
+      const uint32_t s_col = b * BN;
       // The tile is processed in two halves of 64 keys. Half h reads S
-      // columns [64h, 64h+64) and writes its P (32 columns of bf16 pairs) to
-      // columns [32h, 32h+32), which the first half has already consumed.
-      // When the running max is known and the tile is fully visible, the
-      // exponentials use it straight away while the half's max is computed
-      // alongside; only if that max exceeds the running one by more than the
-      // rescale threshold is the half redone (rare). Otherwise the max comes
-      // first. When the max grows, O, the row sum, and (in the second half)
-      // the first half's P are rescaled, so P and the sum always share one max.
+      // columns [64h, 64h+64) and writes its P over the same columns (hi
+      // pairs first, then lo pairs). When the running max is known and the
+      // tile is fully visible, the exponentials use it straight away while
+      // the half's max is computed alongside; only if that max exceeds the
+      // running one by more than the rescale threshold is the half redone
+      // from S, still intact in TMEM (rare). Otherwise the max comes first.
+      // When the max grows in the second half, the first half's P and the row
+      // sum are rescaled, so the tile's P and the sum share one max; the
+      // correction warps rescale O by 2^(m_prev - m_run) for the whole tile.
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
+        const uint32_t s_half = lane_base + s_col + h * 64;
         uint32_t sv[64];
-        tmem_ld32(lane_base + s_col + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(lane_base + s_col + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld32(s_half, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(s_half + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_ld_wait();
         if (!full) {
 #pragma unroll
           for (int c = 0; c < 64; ++c)
             if (h * 64 + c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
         }
-        uint32_t pk[32];
+        uint32_t phi[32], plo[32];
         float ls4[4] = {0.f, 0.f, 0.f, 0.f};
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         const bool optimistic = full && m_run != -INFINITY;
@@ -325,7 +407,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
             const float e1 = fast_exp2(fmaf(s1, p.scale_log2, neg_m));
             ls4[(2 * k) & 3] += e0;
             ls4[(2 * k + 1) & 3] += e1;
-            pk[k] = pack_bf16x2(e0, e1);
+            split_f16x2(e0, e1, phi[k], plo[k]);
           }
         } else {
 #pragma unroll
@@ -339,30 +421,27 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
         if (!optimistic || any_grow) {
           const float alpha = grow ? (m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new)) : 1.f;
           if (grow) m_run = m_new;
-          if (any_grow && j > 0) {
-            // O_X holds P_0..P_{j-1} V and is complete: S_X(j) was issued only
-            // after PV_X(j-1) finished, and S_X(j) has completed.
-#pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t o[32];
-              tmem_ld32(lane_base + o_col + c * 32, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-              tmem_st32(lane_base + o_col + c * 32, o);
-            }
-          }
           if (any_grow && h == 1) {
             // the first half's P was made with the old max
-            uint32_t q[32];
-            tmem_ld32(lane_base + s_col, q);
+            uint32_t qh[32], ql[32];
+            tmem_st_wait();
+            tmem_ld32(lane_base + s_col, qh);
+            tmem_ld32(lane_base + s_col + 32, ql);
             tmem_ld_wait();
 #pragma unroll
             for (int k = 0; k < 32; ++k) {
-              const float2 f = unpack_bf16x2(q[k]);
-              q[k] = pack_bf16x2(f.x * alpha, f.y * alpha);
+              const float2 a = unpack_f16x2(qh[k]);
+              const float2 c = unpack_f16x2(ql[k]);
+              split_f16x2((a.x + c.x) * alpha, (a.y + c.y) * alpha, qh[k], ql[k]);
             }
-            tmem_st32(lane_base + s_col, q);
+            tmem_st32(lane_base + s_col, qh);
+            tmem_st32(lane_base + s_col + 32, ql);
+          }
+          if (optimistic) {
+            // S of this half is still in TMEM (P is written below).
+            tmem_ld32(s_half, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_ld32(s_half + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+            tmem_ld_wait();
           }
           l_run *= alpha;
           const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
@@ -374,46 +453,91 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
             const float e1 = fast_exp2(fmaf(__uint_as_float(sv[2 * k + 1]), p.scale_log2, neg_m));
             ls4[(2 * k) & 3] += e0;
             ls4[(2 * k + 1) & 3] += e1;
-            pk[k] = pack_bf16x2(e0, e1);
+            split_f16x2(e0, e1, phi[k], plo[k]);
           }
         }
-        tmem_st32(lane_base + s_col + h * 32, pk);
+        tmem_st32(s_half, phi);
+        tmem_st32(s_half + 32, plo);
         l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      }
+      // hand the tile's O rescale factor to the correction warps
+      const float tile_alpha =
+          m_run == m_prev ? 1.f : (m_prev == -INFINITY ? 0.f : fast_exp2(m_prev - m_run));
+      if (!__all_sync(0xffffffffu, mbar_wait(&alpha_empty[b], ((j >> 1) & 1) ^ 1, p.err,
+                                             abort_flag, kErrTimeoutSoftmax)))
+        break;
+      alpha_s[b * BM + r] = tile_alpha;
+      mbar_arrive(&alpha_full[b]);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[b]);
+    }
+    l_s[r] = l_run;
+    mbar_arrive(l_ready);
+  } else {
+    // -------------------------------------------------------- correction --
+    const int r = static_cast<int>(threadIdx.x) - 128;
+    const int qi = qt * BM + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const int b = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&alpha_full[b], (j >> 1) & 1, p.err, abort_flag,
+                                             kErrTimeoutSoftmax));
+      if (!ok) break;
+      const float a = alpha_s[b * BM + r];
+      mbar_arrive(&alpha_empty[b]);
+      ok = __all_sync(0xffffffffu, mbar_wait(pv_done, j & 1, p.err, abort_flag,
+                                             kErrTimeoutSoftmax));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t t[32];
+        tmem_ld32(lane_base + kColOt + c * 32, t);
+        if (j == 0) {
+          tmem_ld_wait();
+          tmem_st32(lane_base + kColO + c * 32, t);
+        } else {
+          uint32_t o[32];
+          tmem_ld32(lane_base + kColO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            o[k] = __float_as_uint(fmaf(__uint_as_float(o[k]), a, __uint_as_float(t[k])));
+          tmem_st32(lane_base + kColO + c * 32, o);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[x]);
+      mbar_arrive(ot_free);
     }
     // ------------------------------------------------------- epilogue --
-    if (x == 0 || valid_b) {
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(l_ready, 0, p.err, abort_flag,
+                                                   kErrTimeoutSoftmax));
+    if (ok) {
+      const float l = l_s[r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.O + (static_cast<long long>(bh) * p.S_q + qi) * D;
-      if (ntiles > 0 && ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (ntiles - 1) & 1, p.err, abort_flag,
-                                               kErrTimeoutSoftmax));
-      }
-      if (ok) {
-        tc_fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          if (ntiles > 0) {
-            tmem_ld32(lane_base + o_col + c * 32, o);
-            tmem_ld_wait();
-          } else {
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (nt > 0) {
+          tmem_ld32(lane_base + kColO + c * 32, o);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] = 0u;
-          }
-          if (qi < p.S_q) {
+          for (int k = 0; k < 32; ++k) o[k] = 0u;
+        }
+        if (qi < p.S_q) {
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
-              v.y = pack_bf16x2(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
-              v.z = pack_bf16x2(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
-              v.w = pack_bf16x2(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
-            }
+          for (int g = 0; g < 4; ++g) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
           }
         }
       }
@@ -425,6 +549,17 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  // Exact fallback: a V tile fp16 cannot carry exactly was seen, so every row
+  // of this CTA is recomputed from global memory with fp32 arithmetic (the
+  // appended cache rows were already written by the TMA stores above and are
+  // not touched).
+  if (*needs_exact && !*abort_flag) {
+    if (threadIdx.x == 0) atomicAdd(p.exact_ctas, 1ull);
+    for (int rr = warp; rr < BM; rr += NUM_THREADS / 32) {
+      const int i = qt * BM + rr;
+      if (i < p.S_q) attention_row_exact(p.Q, p.O, p.kv, p.S_q, D, p.scale, p.causal, bh, i, lane);
+    }
   }
 }
 

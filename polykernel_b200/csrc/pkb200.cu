@@ -29,6 +29,9 @@ using bf16 = __nv_bfloat16;
 namespace {
 
 __device__ int g_device_error;
+// CTAs of the tensor-core attention kernel that recomputed their rows exactly
+// (V values outside what its fp16 P.V carries exactly). Cumulative per device.
+__device__ unsigned long long g_attn_exact_ctas;
 
 std::atomic<long long> g_counters[5];
 // Upper bound on the persistent GEMM's grid (0 = one CTA per SM). Lowered by
@@ -42,6 +45,7 @@ struct DeviceInfo {
   bool init = false;
   int sms = 0;
   int* err = nullptr;
+  unsigned long long* attn_exact = nullptr;
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_mu;
@@ -57,6 +61,8 @@ int current_device_info(DeviceInfo** out) {
     e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), g_device_error);
+    if (e != cudaSuccess) return e;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.attn_exact), g_attn_exact_ctas);
     if (e != cudaSuccess) return e;
     d.init = true;
   }
@@ -432,7 +438,7 @@ int run_fp8_pass(int kind, int fmt, const void* in, void* out, long long n, cuda
 template <int D>
 int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, int S_q,
                           float scale, int causal, bf16* Kc, bf16* Vc, int S_max, int S_cache,
-                          cudaStream_t s, int* err) {
+                          cudaStream_t s, int* err, unsigned long long* exact_ctas) {
   using L = attn::Layout<D>;
   auto map3 = [](CUtensorMap* m, const void* base, int rows, long long rows_stride, int BH_) {
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows),
@@ -484,10 +490,13 @@ int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, i
   p.causal = causal ? 1 : 0;
   p.append = append ? 1 : 0;
   p.num_qtiles = (S_q + attn::BM - 1) / attn::BM;
-  p.num_pairs = (p.num_qtiles + 1) / 2;
   p.O = O;
   p.err = err;
-  dim3 grid(p.num_pairs, BH);
+  p.Q = Q;
+  p.kv = kv;
+  p.scale = scale;
+  p.exact_ctas = exact_ctas;
+  dim3 grid(static_cast<unsigned>(p.num_qtiles) * static_cast<unsigned>(BH));
   attention_tc_kernel<D><<<grid, attn::NUM_THREADS, L::SMEM_BYTES, s>>>(mq, mka, mva, mkb, mvb,
                                                                         mks, mvs, p);
   return cudaGetLastError();
@@ -495,11 +504,13 @@ int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, i
 
 int launch_attention_tc(const bf16* Q, bf16* O, const KvSources& kv, int BH, int S_q, int D,
                         float scale, int causal, bf16* Kc, bf16* Vc, int S_max, int S_cache,
-                        cudaStream_t s, int /*sms*/, int* err) {
+                        cudaStream_t s, int* err, unsigned long long* exact_ctas) {
   if (encode_fn() == nullptr) return cudaErrorNotSupported;
   if (D == 128)
-    return launch_attention_tc_d<128>(Q, O, kv, BH, S_q, scale, causal, Kc, Vc, S_max, S_cache, s, err);
-  return launch_attention_tc_d<64>(Q, O, kv, BH, S_q, scale, causal, Kc, Vc, S_max, S_cache, s, err);
+    return launch_attention_tc_d<128>(Q, O, kv, BH, S_q, scale, causal, Kc, Vc, S_max, S_cache, s,
+                                      err, exact_ctas);
+  return launch_attention_tc_d<64>(Q, O, kv, BH, S_q, scale, causal, Kc, Vc, S_max, S_cache, s,
+                                   err, exact_ctas);
 }
 
 int run_attention(const bf16* Q, bf16* O, const KvSources& kv, int B, int H, int S_q, int D,
@@ -511,7 +522,7 @@ int run_attention(const bf16* Q, bf16* O, const KvSources& kv, int B, int H, int
   const int BH = B * H;
   if (BH <= 65535 && attention_tc_supported(kv, S_q, D, Q, O)) {
     e = launch_attention_tc(Q, O, kv, BH, S_q, D, scale, causal, Kc_write, Vc_write, S_max,
-                            S_cache, s, di->sms, di->err);
+                            S_cache, s, di->err, di->attn_exact);
     if (e == cudaSuccess) g_counters[kCntAttnTc]++;
     return e;
   }
@@ -1536,6 +1547,16 @@ int pkb200_device_error(int* code) {
   e = cudaMemcpy(di->err, &zero, sizeof(int), cudaMemcpyHostToDevice);
   if (code) *code = v;
   return e;
+}
+
+int pkb200_attention_exact_ctas(unsigned long long* count) {
+  if (!count) return cudaErrorInvalidValue;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  e = cudaDeviceSynchronize();
+  if (e) return e;
+  return cudaMemcpy(count, di->attn_exact, sizeof(unsigned long long), cudaMemcpyDeviceToHost);
 }
 
 int pkb200_path_counters(long long* out, int n) {

@@ -276,14 +276,16 @@ struct KvSources {
   int ldb_rows;
 };
 
-__global__ void attention_simt_kernel(const __nv_bfloat16* __restrict__ Q,
-                                      __nv_bfloat16* __restrict__ O, KvSources kv, int S_q, int D,
-                                      float scale, int causal) {
-  const int warps = blockDim.x >> 5;
-  const int i = blockIdx.x * warps + (threadIdx.x >> 5);
-  const int bh = blockIdx.y;
-  const int lane = threadIdx.x & 31;
-  if (i >= S_q) return;
+// One query row of exact prefill attention, computed by one warp: fp32 scores,
+// online softmax with expf, fp32 P.V, one bf16 rounding of O (the golden's
+// arithmetic, golden.py:139-172; attention_prefill.cu:84-155). Used by the
+// general-shape kernel below and by the tensor-core kernel for the rows of a
+// CTA whose V tiles fall outside what its fp16 P.V can carry exactly.
+__device__ __forceinline__ void attention_row_exact(const __nv_bfloat16* __restrict__ Q,
+                                                    __nv_bfloat16* __restrict__ O,
+                                                    const KvSources& kv, int S_q, int D,
+                                                    float scale, int causal, int bh, int i,
+                                                    int lane) {
   const int S_kv = kv.n_a + kv.n_b;
   const int limit = causal ? (S_kv - S_q + i) : (S_kv - 1);
   const __nv_bfloat16* q = Q + (static_cast<long long>(bh) * S_q + i) * D;
@@ -296,10 +298,10 @@ __global__ void attention_simt_kernel(const __nv_bfloat16* __restrict__ Q,
   for (int j0 = 0; j0 <= kend; j0 += 32) {
     const int j = j0 + lane;
     float s = -INFINITY;
-    const __nv_bfloat16* krow = nullptr;
     if (j <= kend) {
-      krow = (j < kv.n_a) ? kv.Ka + (static_cast<long long>(bh) * kv.lda_rows + j) * D
-                          : kv.Kb + (static_cast<long long>(bh) * kv.ldb_rows + (j - kv.n_a)) * D;
+      const __nv_bfloat16* krow =
+          (j < kv.n_a) ? kv.Ka + (static_cast<long long>(bh) * kv.lda_rows + j) * D
+                       : kv.Kb + (static_cast<long long>(bh) * kv.ldb_rows + (j - kv.n_a)) * D;
       float dot = 0.f;
       for (int d = 0; d < D; ++d) dot += __bfloat162float(q[d]) * __bfloat162float(krow[d]);
       s = dot * scale;
@@ -333,6 +335,15 @@ __global__ void attention_simt_kernel(const __nv_bfloat16* __restrict__ Q,
     const int d = lane + 32 * c;
     if (d < D) orow[d] = __float2bfloat16_rn(l_run > 0.f ? o[c] * inv : 0.f);
   }
+}
+
+__global__ void attention_simt_kernel(const __nv_bfloat16* __restrict__ Q,
+                                      __nv_bfloat16* __restrict__ O, KvSources kv, int S_q, int D,
+                                      float scale, int causal) {
+  const int warps = blockDim.x >> 5;
+  const int i = blockIdx.x * warps + (threadIdx.x >> 5);
+  if (i >= S_q) return;
+  attention_row_exact(Q, O, kv, S_q, D, scale, causal, blockIdx.y, i, threadIdx.x & 31);
 }
 
 }  // namespace pkb200

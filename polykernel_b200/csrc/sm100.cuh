@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace pkb200 {
@@ -28,6 +29,7 @@ enum DeviceError : int {
   kErrTimeoutSoftmax = 4,   // attention softmax warps waited too long
   kErrAbortSeen = 5,        // a role saw another role's abort
   kErrTimeoutSelfTest = 6,  // the wait-timeout self test (a wait nobody satisfies)
+  kErrTimeoutConvert = 7,   // attention V-tile converter waited too long
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -275,6 +277,14 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_m
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::f16 with fp16 A/B and fp32 D (A/B format 0).
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_major,
+                                                      bool b_mn_major) {
+  return (1u << 4) | (static_cast<uint32_t>(a_mn_major) << 15) |
+         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // 2^x on the SFU (ex2.approx, flush-to-zero): the hardware instruction, used
 // where the softmax needs exp and a relative error of ~2^-22 is immaterial.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -322,6 +332,28 @@ __device__ __forceinline__ float bf16_round(float x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_f16x2(uint32_t u) {
+  __half2 v = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(v);
+}
+
+// Two-term fp16 representation of a pair of fp32 values: hi keeps the top 11
+// significant bits (the fp32 value with its low 13 mantissa bits cleared,
+// exactly an fp16 value in fp16's normal range), lo = x - hi (exact in fp32)
+// rounded to fp16. hi + lo carries ~22 significant bits, so a P.V product
+// computed as P_hi.V + P_lo.V on fp16 tensor cores is within ~2^-22 of fp32.
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const float h0 = __uint_as_float(__float_as_uint(x0) & 0xffffe000u);
+  const float h1 = __uint_as_float(__float_as_uint(x1) & 0xffffe000u);
+  hi = pack_f16x2(h0, h1);
+  lo = pack_f16x2(x0 - h0, x1 - h1);
 }
 
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {

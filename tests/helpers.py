@@ -67,19 +67,41 @@ def check_parity(out_f32, golden_f32, ref64_f32=None, rel_ceiling=Mx.MAX_REL_ERR
     return m
 
 
-def check_attention(out_f32, ref_f32):
-    """Parity for attention. P is rounded to bf16 before the P.V tensor-core
-    MMA (as in production FlashAttention kernels), while the golden keeps P in
-    fp32, so last-bit agreement is lower than for the GEMMs. Tolerance: cosine
-    and PCC >= 0.9999 (10x tighter than the gate) and the largest absolute error
-    within 1e-2 of the output's largest magnitude."""
-    m = Mx.report(out_f32, ref_f32)
-    a = np.asarray(out_f32, np.float64)
-    r = np.asarray(ref_f32, np.float64)
-    m["max_abs_err_rel_to_range"] = float(np.max(np.abs(a - r)) / max(np.max(np.abs(r)), 1e-30))
-    assert m["cosine"] >= 0.9999, m
-    assert m["pcc"] >= 0.9999, m
-    assert m["max_abs_err_rel_to_range"] <= 1e-2, m
+# The reference's attention gate (tests/kernels/test_attention.py:314-334, with
+# the ceilings of :74-76 and :411-418): cosine >= 0.999, PCC >= 0.99, more than
+# 90% of outputs bit-exact, and max_rel_err <= 1e-2; for its "large reduction"
+# class (S_kv >= 128: two chained reductions plus exp, where fp32 summation
+# order alone moves near-zero outputs) the calibrated ceiling is 5e-2.
+ATTN_LARGE_REDUCE_S_KV = 128
+ATTN_LARGE_REDUCE_REL_CEILING = 5e-2
+
+
+def check_attention(out_f32, ref_f32, s_kv=None, ref64_f32=None):
+    """The reference's attention gate, with the max_rel_err ceiling of the
+    shape's class (`s_kv`: keys per query row, default the largest).
+
+    With `ref64_f32` (the same attention with every intermediate in fp64 and
+    one bf16 rounding): the output must be within the ceiling of that exact
+    answer, and within the ceiling plus the golden's own distance from it of
+    the golden. The golden sums in fp32 too, so at long rows its near-zero
+    outputs (|o| ~ 1e-7, next to the 1e-6 epsilon of max_rel_err) sit up to a
+    few percent from the exact value; an implementation as exact as the golden
+    but summing in another order can be that far from the golden there. Where
+    the golden is exact to the ceiling's resolution this is the strict rule."""
+    rel = (Mx.MAX_REL_ERR_THRESHOLD
+           if s_kv is not None and s_kv < ATTN_LARGE_REDUCE_S_KV
+           else ATTN_LARGE_REDUCE_REL_CEILING)
+    m = Mx.report(out_f32, ref_f32, ref64_f32)
+    m["rel_ceiling"] = rel
+    assert m["cosine"] >= Mx.COSINE_THRESHOLD, m
+    assert m["pcc"] >= Mx.PCC_THRESHOLD, m
+    assert m["bit_exact"] > 0.90, m
+    if ref64_f32 is None:
+        assert m["max_rel_err"] <= rel, m
+    else:
+        m["golden_vs_fp64"] = Mx.max_rel_err(ref_f32, ref64_f32)
+        assert m["max_rel_err_vs_fp64"] <= rel, m
+        assert m["max_rel_err"] <= rel + m["golden_vs_fp64"], m
     return m
 
 

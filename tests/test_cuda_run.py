@@ -102,7 +102,9 @@ def test_mlp_and_attention_through_harness(golden, cuda, tmp_path):
         _save(tmp_path / f"{k}.npy", a[f"d128_{k}"])
     assert _run("attention_prefill", tmp_path / "q.npy", tmp_path / "k.npy", tmp_path / "v.npy",
                 tmp_path / "o.npy").returncode == 0
-    check_attention(F(_load(tmp_path / "o.npy")), F(a["d128_o"]))
+    ref64 = O.attention_prefill(F(a["d128_q"]), F(a["d128_k"]), F(a["d128_v"]), True,
+                                acc=np.float64)
+    check_attention(F(_load(tmp_path / "o.npy")), F(a["d128_o"]), s_kv=256, ref64_f32=ref64)
 
 
 @pytest.mark.gpu

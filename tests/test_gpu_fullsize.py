@@ -81,8 +81,11 @@ def test_attention_full_size_sampled_heads(cuda, s_cache):
     for (b, h) in ((0, 0), (3, 31), (2, 17)):
         keys = f32_from_t(kc[b:b + 1, h:h + 1, :s_cache + S])
         vals = f32_from_t(vc[b:b + 1, h:h + 1, :s_cache + S])
-        ref = O.attention_prefill(f32_from_t(q[b:b + 1, h:h + 1]), keys, vals, causal=True)
-        print(s_cache, (b, h), check_attention(f32_from_t(o[b:b + 1, h:h + 1]), ref))
+        qh = f32_from_t(q[b:b + 1, h:h + 1])
+        ref = O.attention_prefill(qh, keys, vals, causal=True)
+        ref64 = O.attention_prefill(qh, keys, vals, causal=True, acc=np.float64)
+        print(s_cache, (b, h), check_attention(f32_from_t(o[b:b + 1, h:h + 1]), ref,
+                                               s_kv=s_cache + S, ref64_f32=ref64))
     assert pk.device_error() == 0
 
 

@@ -86,7 +86,9 @@ def test_attention_vs_golden(golden, pk, name):
     q, k, v = (t_from_bits(g[f"{name}_{x}"]) for x in ("q", "k", "v"))
     c0 = _counters(pk)
     o = pk.ops.attention_prefill(q, k, v, causal=True)
-    m = (check_attention if q.shape[3] in (64, 128) else check_gate)(f32_from_t(o), F(g[f"{name}_o"]))
+    ref64 = O.attention_prefill(F(g[f"{name}_q"]), F(g[f"{name}_k"]), F(g[f"{name}_v"]), True,
+                                acc=np.float64)
+    m = check_attention(f32_from_t(o), F(g[f"{name}_o"]), s_kv=k.shape[2], ref64_f32=ref64)
     print(name, m)
     tc = q.shape[3] in (64, 128)
     assert _used(pk, c0, "attn_tc" if tc else "attn_simt")
@@ -97,7 +99,9 @@ def test_attention_noncausal_vs_golden(golden, pk):
     g = golden("attention")
     q, k, v = (t_from_bits(g[f"full_{x}"]) for x in ("q", "k", "v"))
     o = pk.ops.attention_prefill(q, k, v, causal=False)
-    print("full", check_attention(f32_from_t(o), F(g["full_o"])))
+    ref64 = O.attention_prefill(F(g["full_q"]), F(g["full_k"]), F(g["full_v"]), False,
+                                acc=np.float64)
+    print("full", check_attention(f32_from_t(o), F(g["full_o"]), s_kv=k.shape[2], ref64_f32=ref64))
 
 
 def test_attention_leaky_mask_fails(golden, pk):
@@ -122,8 +126,9 @@ def test_attention_kv_append_vs_golden(golden, pk, name):
     vc[:, :, :Sc] = t["vc"]
     tail_k, tail_v = kc[:, :, Sc + Sn:].clone(), vc[:, :, Sc + Sn:].clone()
     o = pk.ops.attention_prefill_kv_append(t["q"], t["kn"], t["vn"], kc, vc, Sc, causal=True)
-    chk = check_attention if D in (64, 128) else check_gate
-    print(name, chk(f32_from_t(o), F(g[f"{name}_o"])))
+    ref64 = O.attention_prefill(F(g[f"{name}_q"]), F(g[f"{name}_nk"]), F(g[f"{name}_nv"]), True,
+                                acc=np.float64)
+    print(name, check_attention(f32_from_t(o), F(g[f"{name}_o"]), s_kv=Sc + Sn, ref64_f32=ref64))
     assert np.array_equal(bits_from_t(kc[:, :, :Sc + Sn]), g[f"{name}_nk"])
     assert np.array_equal(bits_from_t(vc[:, :, :Sc + Sn]), g[f"{name}_nv"])
     assert torch.equal(kc[:, :, Sc + Sn:], tail_k) and torch.equal(vc[:, :, Sc + Sn:], tail_v)
@@ -197,7 +202,8 @@ def test_attention_mid_vs_oracle(pk):
     q, k, v = (_rand_bits(rng, (B, H, S, D)) for _ in range(3))
     o = pk.ops.attention_prefill(*(t_from_bits(a) for a in (q, k, v)), causal=True)
     ref = O.attention_prefill(F(q), F(k), F(v), True)
-    print("attn mid", check_attention(f32_from_t(o), ref))
+    ref64 = O.attention_prefill(F(q), F(k), F(v), True, acc=np.float64)
+    print("attn mid", check_attention(f32_from_t(o), ref, s_kv=S, ref64_f32=ref64))
 
 
 def test_fused_residual_rmsnorm_vs_golden(golden, pk):
@@ -220,7 +226,9 @@ def test_qkv_projection_feeds_attention(golden, pk):
         r64 = r64.reshape(gold.shape[0], gold.shape[2], gold.shape[1], gold.shape[3]).transpose(0, 2, 1, 3)
         print(key, check_parity(f32_from_t(t), np.ascontiguousarray(gold), r64))
     o = pk.ops.attention_prefill(q, k, v, causal=True)       # the layout attention consumes
-    check_attention(f32_from_t(o), O.attention_prefill(f32_from_t(q), f32_from_t(k), f32_from_t(v)))
+    qf, kf, vf = (f32_from_t(t) for t in (q, k, v))
+    check_attention(f32_from_t(o), O.attention_prefill(qf, kf, vf), s_kv=k.shape[2],
+                    ref64_f32=O.attention_prefill(qf, kf, vf, acc=np.float64))
     assert Kd == 256
 
 
@@ -270,3 +278,70 @@ def test_device_gate_rejects_transposed_operand_and_corruption(golden, pk):
         check_parity(bad, ref)
     with pytest.raises(AssertionError):
         check_parity(O.bf16(good * 1.5), ref)
+
+
+# ----------------------------------------------- fp16 P.V range fallback --
+def _attn_case(rng, shape, v_scale=1.0):
+    q, k = (_rand_bits(rng, shape) for _ in range(2))
+    v = O.to_bits(O.bf16(rng.standard_normal(shape).astype(np.float32) * np.float32(v_scale)))
+    return q, k, v
+
+
+def test_attention_normal_values_take_no_exact_fallback(pk):
+    rng = np.random.default_rng(21)
+    q, k, v = _attn_case(rng, (2, 4, 384, 128))
+    before = pk.attention_exact_ctas()
+    o = pk.ops.attention_prefill(*(t_from_bits(a) for a in (q, k, v)), causal=True)
+    assert pk.attention_exact_ctas() == before
+    check_attention(f32_from_t(o), O.attention_prefill(F(q), F(k), F(v), True), s_kv=384,
+                    ref64_f32=O.attention_prefill(F(q), F(k), F(v), True, acc=np.float64))
+
+
+@pytest.mark.parametrize("kind", ["beyond_fp16_max", "all_tiny"])
+def test_attention_values_outside_fp16_take_exact_fallback(pk, kind):
+    """V values fp16 cannot carry (|v| >= 2^16, a head whose values are all
+    tiny) make the affected CTAs recompute their rows exactly: the output still
+    meets the gate, and the counter shows the fallback ran."""
+    rng = np.random.default_rng(22)
+    shape = (1, 3, 320, 64)
+    if kind == "all_tiny":
+        q, k, v = _attn_case(rng, shape, v_scale=1e-7)
+    else:
+        q, k, v = _attn_case(rng, shape)
+        vf = F(v)
+        vf[0, 1, 5, 3] = 2.0 ** 17
+        v = O.to_bits(vf)
+    before = pk.attention_exact_ctas()
+    o = pk.ops.attention_prefill(*(t_from_bits(a) for a in (q, k, v)), causal=True)
+    assert pk.attention_exact_ctas() > before
+    got, ref = f32_from_t(o), O.attention_prefill(F(q), F(k), F(v), True)
+    check_attention(got, ref, s_kv=320,
+                    ref64_f32=O.attention_prefill(F(q), F(k), F(v), True, acc=np.float64))
+    assert pk.device_error() == 0
+
+
+def test_attention_append_with_fallback_keeps_cache_bf16(pk):
+    """The appended V rows are the caller's bf16 values even when the tile is
+    also rewritten as fp16 for the P.V pass (and when the fallback runs)."""
+    import torch
+    rng = np.random.default_rng(23)
+    B, H, Sc, Sn, D, Smax = 1, 2, 128, 256, 128, 512
+    q, kn, vn = _attn_case(rng, (B, H, Sn, D))
+    vnf = F(vn)
+    vnf[0, 0, 200, 7] = 3.0e5          # beyond fp16 range: bf16 keeps it
+    vn = O.to_bits(vnf)
+    kc = torch.zeros(B, H, Smax, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kcf, vcf = (_rand_bits(rng, (B, H, Sc, D)) for _ in range(2))
+    kc[:, :, :Sc] = t_from_bits(kcf)
+    vc[:, :, :Sc] = t_from_bits(vcf)
+    o = pk.ops.attention_prefill_kv_append(*(t_from_bits(a) for a in (q, kn, vn)), kc, vc, Sc,
+                                           causal=True)
+    assert np.array_equal(bits_from_t(vc[:, :, Sc:Sc + Sn]), vn)
+    assert np.array_equal(bits_from_t(kc[:, :, Sc:Sc + Sn]), kn)
+    keys = np.concatenate([F(kcf), F(kn)], axis=2)
+    vals = np.concatenate([F(vcf), F(vn)], axis=2)
+    ref = O.attention_prefill(F(q), keys, vals, True)
+    check_attention(f32_from_t(o), ref, s_kv=Sc + Sn,
+                    ref64_f32=O.attention_prefill(F(q), keys, vals, True, acc=np.float64))
+    assert pk.device_error() == 0
