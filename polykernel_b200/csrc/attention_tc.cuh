@@ -7,31 +7,36 @@
 // causal (attention_prefill.cu:103), softmax in fp32, P.V accumulated in fp32,
 // one bf16 rounding of O. Rows that see no key produce 0 (attention_prefill.cu:154).
 //
-// One CTA per (128-query tile, batch*head), longest tiles first. Roles (384
+// One CTA per (128-query tile, batch*head), longest tiles first. Roles (512
 // threads):
-//   warps 0-3  softmax. Thread r owns query row r (= TMEM lane r). It reads
-//              its S row with tcgen05.ld, keeps the running max/sum in the
-//              exp2 domain, and writes P back over the same TMEM columns as an
-//              fp16 pair per probability (P = P_hi + P_lo, ~22 significant
-//              bits), where the P.V MMAs read it as their A operand. Per key
-//              tile it hands the row's rescale factor (2^(m_old - m_new)) to
-//              the correction warps.
-//   warps 4-7  correction. Each key tile's P.V lands in a fresh TMEM
+//   warps 0-7  softmax. Warp w of group h (warps 4h..4h+3) handles key half h
+//              (64 keys) of every key tile for the query rows of TMEM lane
+//              quarter w%4; thread r owns query row r (= TMEM lane r). It
+//              reads its S values with tcgen05.ld, agrees on the tile's max
+//              with the thread holding the other half of the row (shared
+//              memory + an mbarrier per lane quarter), keeps the running max
+//              and its half of the row sum in the exp2 domain, and writes P
+//              back over the same TMEM columns as an fp16 pair per probability
+//              (P = P_hi + P_lo, ~21 significant bits, built with FMA/ALU
+//              arithmetic so the SFU pipe only runs exp2), where the P.V MMAs
+//              read it as their A operand. Per key tile group 0 hands the row's
+//              rescale factor (2^(m_old - m_new)) to the correction warps.
+//   warps 8-11 correction. Each key tile's P.V lands in a fresh TMEM
 //              accumulator Ot (16 MMA steps deep); thread r folds it into the
 //              running O of row r with fp32 FMAs, O = O * alpha + Ot, in TMEM.
 //              At the end it normalises O by the row sum and stores it.
-//   warp 8     TMA producer: the Q tile once; K and V tiles (128 keys) through
+//   warp 12    TMA producer: the Q tile once; K and V tiles (128 keys) through
 //              2-deep rings. For the append entry point, the CTA whose query
 //              tile matches a tile of new rows also writes those K/V tiles
 //              from shared memory into the cache with TMA stores, so the
 //              append costs no extra HBM read.
-//   warp 9     TMEM owner + single-thread MMA issuer. Per key tile j: S(j+1)
+//   warp 13    TMEM owner + single-thread MMA issuer. Per key tile j: S(j+1)
 //              into the other S buffer (once P.V(j-1) has read it), then
 //              P.V(j) = P_hi.V + P_lo.V into Ot (once the correction warps have
 //              drained Ot). So the tensor core computes S(j+1) while the
 //              softmax works on S(j), and P.V(j) while the softmax works on
 //              S(j+1).
-//   warps 10-11 V converter: each V tile is rewritten in place in shared
+//   warps 14-15 V converter: each V tile is rewritten in place in shared
 //              memory from bf16 to fp16 (same layout, same swizzle) before the
 //              P.V MMAs read it. Every bf16 value in [2^-17, 65280] is exactly
 //              an fp16 value. A tile that holds a value of magnitude >= 2^16
@@ -42,7 +47,7 @@
 //              the tensor-core pass, so the result never depends on fp16 range.
 //
 // Numerics: scores are fp32 (bf16 Q.K on tensor cores), P is fp32 from the
-// SFU exp2 and enters P.V as fp16 hi+lo (relative error ~2^-22), V enters as
+// SFU exp2 and enters P.V as fp16 hi+lo (relative error ~2^-21), V enters as
 // exact fp16, each key tile's P.V accumulates in fp32 on the tensor core over
 // only 128 keys, and the tiles are summed with round-to-nearest fp32 FMAs.
 // Tensor-core accumulation truncates; summing a 2048-key row in one tensor-core
@@ -69,9 +74,15 @@ constexpr int BM = 128;           // query rows per tile (one tile per CTA)
 constexpr int BN = 128;           // keys per tile
 constexpr int KST = 2;            // K pipeline stages
 constexpr int VST = 3;            // V pipeline stages (TMA, then fp16 conversion)
-constexpr int NUM_THREADS = 384;
-constexpr int kConvThreads = 64;  // warps 10-11
+constexpr int NUM_THREADS = 512;
+constexpr int kConvThreads = 64;  // warps 14-15
+constexpr int kWarpProducer = 12, kWarpMma = 13, kWarpConv0 = 14;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Probabilities are formed as 2^7 * p: with the stale-max threshold p <= 2^8,
+// so 2^7 * p <= 2^15 stays inside fp16's range while the values that would
+// fall into fp16's subnormal range shrink by 2^7. The row sum carries the same
+// factor, so O = sum(P.V) / sum(P) is unchanged.
+constexpr float kPScaleLog2 = 7.0f;
 constexpr uint32_t kColOt = 256;  // per-key-tile P.V accumulator
 constexpr uint32_t kColO = 384;   // running O
 
@@ -84,8 +95,9 @@ struct Layout {
   static constexpr int OFF_K = OFF_Q + Q_BYTES;          // KST stages
   static constexpr int OFF_V = OFF_K + KST * KV_BYTES;   // VST stages
   static constexpr int OFF_ALPHA = OFF_V + VST * KV_BYTES;  // float[2][BM]
-  static constexpr int OFF_L = OFF_ALPHA + 2 * BM * 4;     // float[BM]
-  static constexpr int OFF_BAR = OFF_L + BM * 4;
+  static constexpr int OFF_L = OFF_ALPHA + 2 * BM * 4;     // float[2][BM] (per key half)
+  static constexpr int OFF_HMAX = OFF_L + 2 * BM * 4;      // float[2][2][BM]
+  static constexpr int OFF_BAR = OFF_HMAX + 4 * BM * 4;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 };
 }  // namespace attn
@@ -153,6 +165,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
                                              ~static_cast<uintptr_t>(1023));
   float* alpha_s = reinterpret_cast<float*>(smem + L::OFF_ALPHA);
   float* l_s = reinterpret_cast<float*>(smem + L::OFF_L);
+  float* hmax_s = reinterpret_cast<float*>(smem + L::OFF_HMAX);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;            // [KST]
@@ -168,7 +181,8 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   uint64_t* ot_free = pv_done + 1;        // Ot drained into O
   uint64_t* l_ready = ot_free + 1;        // row sums in l_s
   uint64_t* v_stored = l_ready + 1;       // appended V tile read out of smem
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_stored + 1);
+  uint64_t* pair_bar = v_stored + 1;      // [4] the two softmax warps of a lane quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* needs_exact = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -193,19 +207,20 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], BM);
+      mbar_init(&p_full[i], 2 * BM);
       mbar_init(&alpha_full[i], BM);
       mbar_init(&alpha_empty[i], BM);
     }
     mbar_init(pv_done, 1);
     mbar_init(ot_free, BM);
-    mbar_init(l_ready, BM);
+    mbar_init(l_ready, 2 * BM);
     mbar_init(v_stored, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
     *abort_flag = 0;
     *needs_exact = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -214,7 +229,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == kWarpProducer) {
     if (lane == 0 && nt > 0) {
       // -------------------------------------------------------- producer --
       tma_prefetch_desc(&map_q);
@@ -260,7 +275,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
       }
       bulk_wait_group0();
     }
-  } else if (warp == 9) {
+  } else if (warp == kWarpMma) {
     if (lane == 0 && nt > 0) {
       // ------------------------------------------------------ MMA issuer --
       constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
@@ -314,9 +329,9 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
         issue_pv(j);
       }
     }
-  } else if (warp >= 10) {
+  } else if (warp >= kWarpConv0) {
     // ------------------------------------------------------ V converter --
-    const int t = static_cast<int>(threadIdx.x) - 320;
+    const int t = static_cast<int>(threadIdx.x) - 32 * kWarpConv0;
     int appended = 0;
     for (int j = 0; j < nt; ++j) {
       const int st = j % VST;
@@ -349,134 +364,97 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
       const float wmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
       if (lane == 0 && (!(wmax < 65536.f) || (wmax != 0.f && wmax < 0.015625f))) *needs_exact = 1;
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ----------------------------------------------------------- softmax --
-    const int r = static_cast<int>(threadIdx.x);  // query row within the tile == TMEM lane
+    // Warp w of group h (warps 4h..4h+3) owns key half h of every tile for
+    // TMEM lanes 32(w%4)..: thread r handles keys [64h, 64h+64) of query row r.
+    // The two threads of a row agree on the tile's max through shared memory
+    // (pair_bar: the two warps of a lane quarter), so both form P with the
+    // same running max.
+    const int hk = warp >> 2;                     // key half
+    const int r = static_cast<int>(threadIdx.x) & (BM - 1);
     const int qi = qt * BM + r;
     const int S_kv = p.n_a + p.n_b;
     const int limit = p.causal ? (S_kv - p.S_q + qi) : (S_kv - 1);
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    uint64_t* pbar = &pair_bar[warp & 3];
     float m_run = -INFINITY;
-    float l_run = 0.f;
+    float l_run = 0.f;  // this thread's half of the row sum
     for (int j = 0; j < nt; ++j) {
       const int b = j & 1;
       const bool from_a = j < p.tiles_a;
       const int p0 = from_a ? j * BN : p.n_a + (j - p.tiles_a) * BN;
       const int cnt = from_a ? min(BN, p.n_a - j * BN) : min(BN, p.n_b - (j - p.tiles_a) * BN);
-      const int nvalid = max(0, min(cnt, limit - p0 + 1));
+      const int nvalid = max(0, min(cnt, limit - p0 + 1)) - hk * 64;  // keys of this half
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, p.err, abort_flag,
                                              kErrTimeoutSoftmax)))
         break;
       tc_fence_after();
-      const bool full = __all_sync(0xffffffffu, nvalid == BN);
-      const float m_prev = m_run;
-      const uint32_t s_col = b * BN;
-      // The tile is processed in two halves of 64 keys. Half h reads S
-      // columns [64h, 64h+64) and writes its P over the same columns (hi
-      // pairs first, then lo pairs). When the running max is known and the
-      // tile is fully visible, the exponentials use it straight away while
-      // the half's max is computed alongside; only if that max exceeds the
-      // running one by more than the rescale threshold is the half redone
-      // from S, still intact in TMEM (rare). Otherwise the max comes first.
-      // When the max grows in the second half, the first half's P and the row
-      // sum are rescaled, so the tile's P and the sum share one max; the
-      // correction warps rescale O by 2^(m_prev - m_run) for the whole tile.
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t s_half = lane_base + s_col + h * 64;
-        uint32_t sv[64];
-        tmem_ld32(s_half, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(s_half + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld_wait();
-        if (!full) {
+      const uint32_t s_half = lane_base + b * BN + hk * 64;
+      uint32_t sv[64];
+      tmem_ld32(s_half, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld32(s_half + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tmem_ld_wait();
+      if (__any_sync(0xffffffffu, nvalid < 64)) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (h * 64 + c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
-        }
-        uint32_t phi[32], plo[32];
-        float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        const bool optimistic = full && m_run != -INFINITY;
-        if (optimistic) {
-          const float neg_m = -m_run;
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const float s0 = __uint_as_float(sv[2 * k]), s1 = __uint_as_float(sv[2 * k + 1]);
-            mx4[k & 3] = fmax3(mx4[k & 3], s0, s1);
-            const float e0 = fast_exp2(fmaf(s0, p.scale_log2, neg_m));
-            const float e1 = fast_exp2(fmaf(s1, p.scale_log2, neg_m));
-            ls4[(2 * k) & 3] += e0;
-            ls4[(2 * k + 1) & 3] += e1;
-            split_f16x2(e0, e1, phi[k], plo[k]);
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 32; ++k)
-            mx4[k & 3] = fmax3(mx4[k & 3], __uint_as_float(sv[2 * k]), __uint_as_float(sv[2 * k + 1]));
-        }
-        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
-        const float m_new = fmaxf(m_run, mx);
-        const bool grow = m_new > m_run + kRescaleThreshold || (m_run == -INFINITY && m_new > -INFINITY);
-        const bool any_grow = __any_sync(0xffffffffu, grow);
-        if (!optimistic || any_grow) {
-          const float alpha = grow ? (m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new)) : 1.f;
-          if (grow) m_run = m_new;
-          if (any_grow && h == 1) {
-            // the first half's P was made with the old max
-            uint32_t qh[32], ql[32];
-            tmem_st_wait();
-            tmem_ld32(lane_base + s_col, qh);
-            tmem_ld32(lane_base + s_col + 32, ql);
-            tmem_ld_wait();
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const float2 a = unpack_f16x2(qh[k]);
-              const float2 c = unpack_f16x2(ql[k]);
-              split_f16x2((a.x + c.x) * alpha, (a.y + c.y) * alpha, qh[k], ql[k]);
-            }
-            tmem_st32(lane_base + s_col, qh);
-            tmem_st32(lane_base + s_col + 32, ql);
-          }
-          if (optimistic) {
-            // S of this half is still in TMEM (P is written below).
-            tmem_ld32(s_half, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-            tmem_ld32(s_half + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-            tmem_ld_wait();
-          }
-          l_run *= alpha;
-          const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) ls4[q] = 0.f;
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const float e0 = fast_exp2(fmaf(__uint_as_float(sv[2 * k]), p.scale_log2, neg_m));
-            const float e1 = fast_exp2(fmaf(__uint_as_float(sv[2 * k + 1]), p.scale_log2, neg_m));
-            ls4[(2 * k) & 3] += e0;
-            ls4[(2 * k + 1) & 3] += e1;
-            split_f16x2(e0, e1, phi[k], plo[k]);
-          }
-        }
-        tmem_st32(s_half, phi);
-        tmem_st32(s_half + 32, plo);
-        l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+        for (int c = 0; c < 64; ++c)
+          if (c >= nvalid) sv[c] = __float_as_uint(-INFINITY);
       }
-      // hand the tile's O rescale factor to the correction warps
-      const float tile_alpha =
-          m_run == m_prev ? 1.f : (m_prev == -INFINITY ? 0.f : fast_exp2(m_prev - m_run));
-      if (!__all_sync(0xffffffffu, mbar_wait(&alpha_empty[b], ((j >> 1) & 1) ^ 1, p.err,
-                                             abort_flag, kErrTimeoutSoftmax)))
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        mx4[k & 3] = fmax3(mx4[k & 3], __uint_as_float(sv[2 * k]), __uint_as_float(sv[2 * k + 1]));
+      const float mx_half = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+      hmax_s[(b * 2 + hk) * BM + r] = mx_half;
+      mbar_arrive(pbar);
+      if (!__all_sync(0xffffffffu, mbar_wait(pbar, j & 1, p.err, abort_flag, kErrTimeoutSoftmax)))
         break;
-      alpha_s[b * BM + r] = tile_alpha;
-      mbar_arrive(&alpha_full[b]);
+      const float mx = fmaxf(mx_half, hmax_s[(b * 2 + (hk ^ 1)) * BM + r]);
+      // The running max moves only when the tile's max exceeds it by more
+      // than the rescale threshold (both threads of the row decide alike).
+      const float m_prev = m_run;
+      const float m_new = fmaxf(m_run, mx);
+      if (m_new > m_run + kRescaleThreshold || (m_run == -INFINITY && m_new > -INFINITY)) {
+        l_run *= (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float neg_m = (m_run == -INFINITY) ? 0.f : kPScaleLog2 - m_run;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        uint32_t phi[16], plo[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int kk = q * 16 + k;
+          const float e0 = fast_exp2(fmaf(__uint_as_float(sv[2 * kk]), p.scale_log2, neg_m));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(sv[2 * kk + 1]), p.scale_log2, neg_m));
+          ls4[(2 * k) & 3] += e0;
+          ls4[(2 * k + 1) & 3] += e1;
+          split_f16x2(e0, e1, phi[k], plo[k]);
+        }
+        tmem_st16(s_half + q * 16, phi);
+        tmem_st16(s_half + 32 + q * 16, plo);
+      }
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      if (hk == 0) {
+        // hand the tile's O rescale factor to the correction warps
+        const float tile_alpha =
+            m_run == m_prev ? 1.f : (m_prev == -INFINITY ? 0.f : fast_exp2(m_prev - m_run));
+        if (!__all_sync(0xffffffffu, mbar_wait(&alpha_empty[b], ((j >> 1) & 1) ^ 1, p.err,
+                                               abort_flag, kErrTimeoutSoftmax)))
+          break;
+        alpha_s[b * BM + r] = tile_alpha;
+        mbar_arrive(&alpha_full[b]);
+      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[b]);
     }
-    l_s[r] = l_run;
+    l_s[hk * BM + r] = l_run;
     mbar_arrive(l_ready);
   } else {
     // -------------------------------------------------------- correction --
-    const int r = static_cast<int>(threadIdx.x) - 128;
+    const int r = static_cast<int>(threadIdx.x) - 2 * BM;
     const int qi = qt * BM + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     bool ok = true;
@@ -516,7 +494,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(l_ready, 0, p.err, abort_flag,
                                                    kErrTimeoutSoftmax));
     if (ok) {
-      const float l = l_s[r];
+      const float l = l_s[r] + l_s[BM + r];
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.O + (static_cast<long long>(bh) * p.S_q + qi) * D;
 #pragma unroll 1
@@ -546,7 +524,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -236,6 +236,26 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -312,6 +332,11 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -344,16 +369,26 @@ __device__ __forceinline__ float2 unpack_f16x2(uint32_t u) {
   return __half22float2(v);
 }
 
-// Two-term fp16 representation of a pair of fp32 values: hi keeps the top 11
-// significant bits (the fp32 value with its low 13 mantissa bits cleared,
-// exactly an fp16 value in fp16's normal range), lo = x - hi (exact in fp32)
-// rounded to fp16. hi + lo carries ~22 significant bits, so a P.V product
-// computed as P_hi.V + P_lo.V on fp16 tensor cores is within ~2^-22 of fp32.
+// Two-term fp16 representation of a pair of non-negative fp32 values below
+// 2^16. hi keeps the top 11 significant bits (x with its low 13 mantissa bits
+// cleared), lo = x - hi (exact in fp32). lo's fp16 code is built with FMA/ALU
+// arithmetic (a conversion instruction shares the SFU pipe with exp2):
+// it is read off the fp32 bits of v * 2^-112 shifted right by 13:
+// the multiply moves the exponent bias from 127 to 15, and a result below
+// fp32's normal range lands on exactly the fp16 subnormal encoding. The shift
+// truncates, so lo keeps 11 more bits (hi + lo carries ~21 significant bits;
+// values below 2^-14 keep what the fp16 subnormal grid holds).
 __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  constexpr float kRebias = 1.9259299443872359e-34f;  // 2^-112
   const float h0 = __uint_as_float(__float_as_uint(x0) & 0xffffe000u);
   const float h1 = __uint_as_float(__float_as_uint(x1) & 0xffffe000u);
+  const uint64_t l2 = f2_sub(f2_pack(x0, x1), f2_pack(h0, h1));
+  float tl0, tl1;
+  f2_unpack(f2_mul(l2, f2_pack(kRebias, kRebias)), tl0, tl1);
+  // hi is already an fp16 value in fp16's normal range: one pack instruction
+  // converts it exactly (below that range it rounds onto the subnormal grid).
   hi = pack_f16x2(h0, h1);
-  lo = pack_f16x2(x0 - h0, x1 - h1);
+  lo = __byte_perm(__float_as_uint(tl0) >> 13, __float_as_uint(tl1) >> 13, 0x5410);
 }
 
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
