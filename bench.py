@@ -141,7 +141,7 @@ def run_reference_arm(args):
     if missing:
         print(json.dumps({"impl": "reference", "unavailable":
                           f"{', '.join(os.path.relpath(m, ROOT) for m in missing)} not built "
-                          "(make -C oracle)"}))
+                          "(__graft_entry__.build())"}))
         return 0
     threads = host_threads()
     t_mlp = max(1, threads // 2)
@@ -623,6 +623,235 @@ def run_gpu_arm(args):
     return 0
 
 
+
+# ----------------------------------------------------------- profiling aids --
+
+PROFILE_CASES = {
+    "attn": "attention_prefill, BASELINE config 3 (B=4, H=32, S=2048, D=128, causal)",
+    "attn_b1": "attention_prefill, config 3 with B=1 (the ncu capture case)",
+    "gemm1c5": "fused_matmul_bias_gelu at config-5 GEMM1 shape with M=4096 (d=8192, ffn=28672)",
+    "gemm2c5": "matmul + bias + residual (mlp GEMM2 epilogue) at config-5 GEMM2 shape, M=4096",
+    "gemm": "plain matmul 2048 x 4096 x 16384 (config-2 GEMM1 shape)",
+}
+
+
+def run_profile_case(which):
+    """One small single-kernel case for ncu: each runs its kernel three times
+    (profile a later launch with `-s 2 -c 1`)."""
+    import torch
+    import polykernel_b200 as pk
+    dev = "cuda"
+    if which in ("attn", "attn_b1"):
+        q = torch.randn(4 if which == "attn" else 1, 32, 2048, 128, device=dev).bfloat16()
+        k, v = torch.randn_like(q), torch.randn_like(q)
+        for _ in range(3):
+            pk.ops.attention_prefill(q, k, v, True)
+    elif which == "gemm1c5":
+        a = torch.randn(4096, 8192, device=dev).bfloat16()
+        b = (torch.randn(8192, 28672, device=dev) / 90).bfloat16()
+        bias = (0.02 * torch.randn(28672, device=dev)).bfloat16()
+        for _ in range(3):
+            pk.ops.fused_matmul_bias_gelu(a, b, bias)
+    elif which == "gemm2c5":
+        h = torch.randn(4096, 28672, device=dev).bfloat16()
+        w2 = (torch.randn(28672, 8192, device=dev) / 170).bfloat16()
+        b2 = (0.02 * torch.randn(8192, device=dev)).bfloat16()
+        x = torch.randn(4096, 8192, device=dev).bfloat16()
+        for _ in range(3):
+            pk.ops.matmul_bias_residual(h, w2, b2, x)
+    elif which == "gemm":
+        a = torch.randn(2048, 4096, device=dev).bfloat16()
+        b = (torch.randn(4096, 16384, device=dev) / 64).bfloat16()
+        for _ in range(3):
+            pk.ops.matmul(a, b)
+    else:
+        raise SystemExit(f"unknown profile case {which!r}; one of {sorted(PROFILE_CASES)}")
+    torch.cuda.synchronize()
+    assert pk.device_error() == 0
+    print("ok", which, pk.path_counters())
+    return 0
+
+
+# ------------------------------------------------- tensor-parallel breakdown --
+def _tp_time(fn, iters, warmup, dev):
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([s.elapsed_time(e) / iters], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class _TpShared:
+    """A device buffer of this library (pkb200_ipc_alloc) mapped into every
+    peer with CUDA IPC; ptrs[p] is rank p's buffer in this process."""
+
+    def __init__(self, nbytes, world, rank):
+        import torch.distributed as dist
+        from polykernel_b200._lib import check, lib
+        self.lib = lib()
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        check(self.lib.pkb200_ipc_alloc(nbytes, ctypes.byref(own), handle), "ipc_alloc")
+        gathered = [None] * world
+        dist.all_gather_object(gathered, handle.raw)
+        self.ptrs, self.opened, self.own = [], [], own.value
+        for p in range(world):
+            if p == rank:
+                self.ptrs.append(own.value)
+                continue
+            q = ctypes.c_void_p()
+            check(self.lib.pkb200_ipc_open(gathered[p], ctypes.byref(q)), "ipc_open")
+            self.ptrs.append(q.value)
+            self.opened.append(q.value)
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier()
+        for q in self.opened:
+            self.lib.pkb200_ipc_close(q)
+        dist.barrier()
+        self.lib.pkb200_free(self.own)
+
+
+def run_tp_breakdown(args):
+    """Times each part of the tensor-parallel MLP's exchange in isolation at
+    config 5, one process per GPU (launched like the bench itself, under
+    torchrun). Rank 0 prints one JSON line per measurement: {"part", "n_gpus",
+    "ms", "gbs"}. Every time is CUDA-event timed on each rank and reduced as
+    the max over ranks. Byte counts are per rank, outgoing over NVLink:
+    push (N-1)/N * M*d*4 (fp32 partial row blocks to their owners), pull
+    (N-1)/N * M*d*2 (the reduced bf16 rows from every peer). Parts:
+    gemm2_chunked (the window the exchange must hide in), NCCL reduce-scatter
+    of the fp32 partials and all-gather of the bf16 rows, copy-engine push /
+    pull / both with one stream per peer or one for all, the pushes beside
+    the chunked GEMM2, and the whole TensorParallelMLP step per exchange."""
+    import torch
+    import torch.distributed as dist
+    from polykernel_b200._lib import check, lib
+    from polykernel_b200.tp import TensorParallelMLP
+    args.M, args.d, args.ffn, args.chunks = 16384, 8192, 28672, args.tp_chunks
+    args.iters = args.steps
+
+    # separate hardware queues for the per-peer copy streams (before CUDA starts)
+    os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev)
+    M, d, ffn, C = args.M, args.d, args.ffn, args.chunks
+    if ffn % world or M % (C * world):
+        raise SystemExit("ffn must divide by N and M by chunks*N")
+    F = ffn // world
+    per = M // world
+    out = []
+
+    def emit(part, ms, nbytes=None, **extra):
+        rec = {"part": part, "n_gpus": world, "ms": round(ms, 4),
+               "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1) if nbytes else None, **extra}
+        out.append(rec)
+        if rank == 0:
+            print(json.dumps(rec), flush=True)
+
+    g = torch.Generator(device=dev).manual_seed(rank)
+    h = torch.randn(M, F, device=dev, generator=g).to(torch.bfloat16)
+    w2 = (torch.randn(F, d, device=dev, generator=g) / F ** 0.5).to(torch.bfloat16)
+    y32 = torch.empty(M, d, device=dev, dtype=torch.float32)
+    rows = M // C
+    main_s = torch.cuda.current_stream()
+
+    def gemm2_chunks():
+        for i in range(C):
+            check(lib().pkb200_matmul_f32out(h[i * rows:(i + 1) * rows].data_ptr(), w2.data_ptr(),
+                                             y32[i * rows:(i + 1) * rows].data_ptr(), rows, d, F,
+                                             main_s.cuda_stream), "matmul_f32out")
+    emit("gemm2_chunked", _tp_time(gemm2_chunks, args.iters, args.warmup, dev))
+
+    part32 = torch.empty(per, d, device=dev, dtype=torch.float32)
+    y16 = torch.empty(M, d, device=dev, dtype=torch.bfloat16)
+    mine16 = torch.empty(per, d, device=dev, dtype=torch.bfloat16)
+    push_bytes = (world - 1) * per * d * 4
+    pull_bytes = (world - 1) * per * d * 2
+    emit("nccl_reduce_scatter_fp32",
+         _tp_time(lambda: dist.reduce_scatter_tensor(part32, y32), args.iters, args.warmup, dev),
+         push_bytes)
+    emit("nccl_all_gather_bf16",
+         _tp_time(lambda: dist.all_gather_into_tensor(y16, mine16), args.iters, args.warmup, dev),
+         pull_bytes)
+
+    if world > 1:
+        slots = _TpShared(M * d * 4, world, rank)     # [world][per][d] fp32 per rank
+        rows16 = _TpShared(per * d * 2, world, rank)  # [per][d] bf16 per rank
+        streams = [torch.cuda.Stream(dev) for _ in range(world)]
+        peers = [(rank + k) % world for k in range(1, world)]
+
+        def copies(push, pull, per_peer):
+            ev = torch.cuda.Event()
+            ev.record(main_s)
+            for p in peers:
+                s = streams[p if per_peer else 0]
+                s.wait_event(ev)
+                if push:
+                    check(lib().pkb200_copy_async(
+                        slots.ptrs[p] + rank * per * d * 4, y32[p * per:(p + 1) * per].data_ptr(),
+                        per * d * 4, s.cuda_stream), "copy_async")
+                if pull:
+                    check(lib().pkb200_copy_async(
+                        y16[p * per:(p + 1) * per].data_ptr(), rows16.ptrs[p], per * d * 2,
+                        s.cuda_stream), "copy_async")
+            for s in (streams if per_peer else streams[:1]):
+                main_s.wait_stream(s)
+
+        for mode, per_peer in (("per_peer", True), ("one_stream", False)):
+            emit("ce_push", _tp_time(lambda: copies(True, False, per_peer), args.iters,
+                                  args.warmup, dev), push_bytes, streams=mode)
+            emit("ce_pull", _tp_time(lambda: copies(False, True, per_peer), args.iters,
+                                  args.warmup, dev), pull_bytes, streams=mode)
+            emit("ce_push_pull", _tp_time(lambda: copies(True, True, per_peer), args.iters,
+                                       args.warmup, dev), push_bytes + pull_bytes, streams=mode)
+
+        def push_during_gemm():
+            ev = torch.cuda.Event()
+            ev.record(main_s)
+            for p in peers:
+                streams[p].wait_event(ev)
+                check(lib().pkb200_copy_async(
+                    slots.ptrs[p] + rank * per * d * 4, y32[p * per:(p + 1) * per].data_ptr(),
+                    per * d * 4, streams[p].cuda_stream), "copy_async")
+            gemm2_chunks()
+            for p in peers:
+                main_s.wait_stream(streams[p])
+        emit("ce_push_during_gemm", _tp_time(push_during_gemm, args.iters, args.warmup, dev),
+             push_bytes)
+        slots.close()
+        rows16.close()
+
+        x = torch.randn(M, d, device=dev, generator=g).to(torch.bfloat16)
+        gamma = torch.ones(d, device=dev, dtype=torch.bfloat16)
+        w1 = (torch.randn(d, F, device=dev, generator=g) / d ** 0.5).to(torch.bfloat16)
+        b1 = torch.zeros(F, device=dev, dtype=torch.bfloat16)
+        b2 = torch.zeros(d, device=dev, dtype=torch.bfloat16)
+        for reduce in ("nccl", "copy_engine"):
+            m = TensorParallelMLP(gamma, w1, b1, w2, b2, 1e-6, chunks=C, reduce=reduce)
+            y = torch.empty_like(x)
+            emit(f"mlp_step_{reduce}", _tp_time(lambda: m(x, out=y), args.iters, args.warmup, dev))
+            m.close()
+    dist.destroy_process_group()
+    return 0
+
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -647,7 +876,15 @@ def main():
     # (profiles/gemm_tc_bias_gelu_c5_gemm1_m4096.md) x 4 for M=16384 (traffic grows with M).
     ap.add_argument("--traffic", type=float, default=7.19e9,
                     help="DRAM bytes per GEMM1 launch from an ncu capture (scaled)")
+    ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
+                    help="run one small single-kernel case for an ncu capture and exit")
+    ap.add_argument("--tp-breakdown", action="store_true",
+                    help="time each part of the tensor-parallel exchange (under torchrun) and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args.profile_case)
+    if args.tp_breakdown:
+        return run_tp_breakdown(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -9,6 +9,11 @@
  *     append entry is written in place).
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream),
  *     as in the reference's launch_* functions. Launches are asynchronous.
+ *     Entry points may be called from several host threads and streams at
+ *     once; one-time per-device set-up is serialised inside the library. The
+ *     persistent GEMM's dynamic tile schedule takes one of 4096 per-device
+ *     counters per launch, so at most 4096 GEMM launches may be in flight
+ *     (enqueued, not finished) on one device at a time.
  *   - Return value: 0 on success, otherwise a cudaError_t value
  *     (cudaErrorInvalidValue = 1 for a rejected shape/pointer). The reference's
  *     void launch_* functions only print on error (kernel_common.h:160-167);
@@ -159,6 +164,10 @@ int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_sha
                           const void* b2, const void* x, void* out, unsigned int epoch,
                           void* stream);
 int pkb200_tp_ce_wait(void* plan, int timeout_ms);
+/* Number of exchange streams (push, pull and reduce) the last
+ * pkb200_tp_ce_mlp_step joined back into the caller's stream: 2*(world-1)+1
+ * with one push/pull stream per peer, 3 with one shared pair. */
+int pkb200_tp_ce_joined_streams(void* plan, int* count);
 
 /* out = rmsnorm(bf16(x + resid); weight, eps) over the last axis
  * (golden.fused_residual_rmsnorm, tests/golden/golden.py:108-112): the residual

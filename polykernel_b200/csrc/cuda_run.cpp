@@ -168,6 +168,47 @@ std::vector<int64_t> with_last(std::vector<int64_t> s, int64_t last) {
   return s;
 }
 
+// ------------------------------------------------------------ shape checks --
+// Every operand is validated against the primary one before any device
+// allocation, so a mismatched or short file is rejected (exit 1) and no kernel
+// ever reads past a buffer.
+int shape_error(const char* op, const std::string& msg) {
+  std::fprintf(stderr, "[pkb200-cuda_run] %s: shape error: %s\n", op, msg.c_str());
+  return 1;
+}
+
+std::string dims_str(const Npy& a) {
+  std::string s = "(";
+  for (size_t i = 0; i < a.shape.size(); ++i) s += (i ? "," : "") + std::to_string(a.shape[i]);
+  return s + ")";
+}
+
+constexpr int64_t kIntMax = 2147483647;
+
+// Rows x cols view of a matrix operand whose last axis is the contraction /
+// feature axis: rank >= 1, last axis > 0, both fit in int.
+bool rows_cols(const Npy& a, int64_t& rows, int64_t& cols) {
+  if (a.shape.empty() || a.shape.back() <= 0) return false;
+  cols = a.shape.back();
+  rows = a.size() / cols;
+  return rows <= kIntMax && cols <= kIntMax;
+}
+
+// A [K, N] weight: rank 2, K == k, N > 0.
+bool is_kn(const Npy& w, int64_t k) {
+  return w.shape.size() == 2 && w.shape[0] == k && w.shape[1] > 0 && w.shape[1] <= kIntMax;
+}
+
+// A vector of n elements (any rank, as the reference's harness accepts).
+bool is_vec(const Npy& v, int64_t n) { return !v.shape.empty() && v.size() == n; }
+
+bool is_4d(const Npy& a) {
+  if (a.shape.size() != 4) return false;
+  for (int64_t d : a.shape)
+    if (d < 0 || d > kIntMax) return false;
+  return a.shape[3] > 0;
+}
+
 // Optional "--flag value" arguments after the positional ones.
 struct Opts {
   float epsilon = 1e-5f;
@@ -197,13 +238,18 @@ int run_rmsnorm(int argc, char** argv) {
   Opts o = parse_opts(argc, argv, 4);
   if (!o.ok) return usage("rmsnorm IN OUT [--weight W.npy] [--epsilon E]");
   Npy in = read_npy(argv[2], "<V2");
-  const int64_t cols = in.shape.back(), rows = in.size() / cols;
-  Dev din(in), dout(in.bytes.size());
+  int64_t rows = 0, cols = 0;
+  if (!rows_cols(in, rows, cols)) return shape_error("rmsnorm", "input " + dims_str(in));
   Npy w;
+  if (!o.weight.empty()) {
+    w = read_npy(o.weight, "<V2");
+    if (!is_vec(w, cols))
+      return shape_error("rmsnorm", "weight " + dims_str(w) + " != cols " + std::to_string(cols));
+  }
+  Dev din(in), dout(in.bytes.size());
   const void* wp = nullptr;
   std::unique_ptr<Dev> dw;
   if (!o.weight.empty()) {
-    w = read_npy(o.weight, "<V2");
     dw.reset(new Dev(w));
     wp = dw->p;
   }
@@ -249,12 +295,10 @@ int run_softmax(int argc, char** argv) {
 int run_matmul(int argc, char** argv) {
   if (argc != 5) return usage("matmul A B C");
   Npy a = read_npy(argv[2], "<V2"), b = read_npy(argv[3], "<V2");
-  const int64_t K = a.shape.back(), M = a.size() / K, N = b.shape[1];
-  if (b.shape[0] != K) {
-    std::fprintf(stderr, "matmul: contraction mismatch A.K=%lld != B.K=%lld\n", (long long)K,
-                 (long long)b.shape[0]);
-    return 1;
-  }
+  int64_t M = 0, K = 0;
+  if (!rows_cols(a, M, K)) return shape_error("matmul", "A " + dims_str(a));
+  if (!is_kn(b, K)) return shape_error("matmul", "B " + dims_str(b) + " is not [" + std::to_string(K) + ", N]");
+  const int64_t N = b.shape[1];
   Dev da(a), db(b), dc(static_cast<size_t>(M * N) * 2);
   int st = finish(pkb200_matmul(da.p, db.p, dc.p, (int)M, (int)N, (int)K, nullptr), "matmul");
   if (!st) download(dc, with_last(a.shape, N), argv[4]);
@@ -266,15 +310,19 @@ int run_fused_rmsnorm_matmul(int argc, char** argv) {
   Opts o = parse_opts(argc, argv, 5);
   if (!o.ok) return usage("fused_rmsnorm_matmul X W OUT [--epsilon E] [--weight GAMMA.npy]");
   Npy x = read_npy(argv[2], "<V2"), w = read_npy(argv[3], "<V2");
-  const int64_t K = x.shape.back(), M = x.size() / K, N = w.shape[1];
-  if (w.shape[0] != K) {
-    std::fprintf(stderr, "fused_rmsnorm_matmul: K mismatch X.K=%lld != W.K=%lld\n", (long long)K,
-                 (long long)w.shape[0]);
-    return 1;
+  int64_t M = 0, K = 0;
+  if (!rows_cols(x, M, K)) return shape_error("fused_rmsnorm_matmul", "X " + dims_str(x));
+  if (!is_kn(w, K))
+    return shape_error("fused_rmsnorm_matmul", "W " + dims_str(w) + " is not [" + std::to_string(K) + ", N]");
+  const int64_t N = w.shape[1];
+  Npy gm;
+  if (!o.weight.empty()) {
+    gm = read_npy(o.weight, "<V2");
+    if (!is_vec(gm, K)) return shape_error("fused_rmsnorm_matmul", "gamma " + dims_str(gm) + " != K");
   }
   Dev dx(x), dw(w), dout(static_cast<size_t>(M * N) * 2);
   std::unique_ptr<Dev> dg;
-  if (!o.weight.empty()) dg.reset(new Dev(read_npy(o.weight, "<V2")));
+  if (!o.weight.empty()) dg.reset(new Dev(gm));
   int st = finish(pkb200_fused_rmsnorm_matmul(dx.p, dw.p, dg ? dg->p : nullptr, dout.p, (int)M,
                                               (int)N, (int)K, o.epsilon, nullptr),
                   "fused_rmsnorm_matmul");
@@ -285,11 +333,11 @@ int run_fused_rmsnorm_matmul(int argc, char** argv) {
 int run_fused_matmul_bias_gelu(int argc, char** argv) {
   if (argc != 6) return usage("fused_matmul_bias_gelu A B BIAS OUT");
   Npy a = read_npy(argv[2], "<V2"), b = read_npy(argv[3], "<V2"), bias = read_npy(argv[4], "<V2");
-  const int64_t K = a.shape.back(), M = a.size() / K, N = b.shape[1];
-  if (b.shape[0] != K || bias.size() != N) {
-    std::fprintf(stderr, "fused_matmul_bias_gelu: shape mismatch\n");
-    return 1;
-  }
+  int64_t M = 0, K = 0;
+  if (!rows_cols(a, M, K)) return shape_error("fused_matmul_bias_gelu", "A " + dims_str(a));
+  if (!is_kn(b, K)) return shape_error("fused_matmul_bias_gelu", "B " + dims_str(b) + " is not [K, N]");
+  const int64_t N = b.shape[1];
+  if (!is_vec(bias, N)) return shape_error("fused_matmul_bias_gelu", "bias " + dims_str(bias) + " != N");
   Dev da(a), db(b), dbias(bias), dout(static_cast<size_t>(M * N) * 2);
   int st = finish(pkb200_fused_matmul_bias_gelu(da.p, db.p, dbias.p, dout.p, (int)M, (int)N,
                                                 (int)K, nullptr),
@@ -301,11 +349,11 @@ int run_fused_matmul_bias_gelu(int argc, char** argv) {
 int run_matmul_int8(int argc, char** argv) {
   if (argc != 6) return usage("matmul_int8 A WQ SCALE OUT   (A bf16 [M,K], WQ int8 [K,N], SCALE fp32 [N])");
   Npy a = read_npy(argv[2], "<V2"), wq = read_npy(argv[3], "|i1"), sc = read_npy(argv[4], "<f4");
-  const int64_t K = a.shape.back(), M = a.size() / K, N = wq.shape[1];
-  if (wq.shape[0] != K || sc.size() != N) {
-    std::fprintf(stderr, "matmul_int8: shape mismatch\n");
-    return 1;
-  }
+  int64_t M = 0, K = 0;
+  if (!rows_cols(a, M, K)) return shape_error("matmul_int8", "A " + dims_str(a));
+  if (!is_kn(wq, K)) return shape_error("matmul_int8", "WQ " + dims_str(wq) + " is not [K, N]");
+  const int64_t N = wq.shape[1];
+  if (!is_vec(sc, N)) return shape_error("matmul_int8", "SCALE " + dims_str(sc) + " != N");
   Dev da(a), dw(wq), ds(sc), dout(static_cast<size_t>(M * N) * 2);
   int st = finish(pkb200_matmul_int8(da.p, static_cast<const int8_t*>(dw.p),
                                      static_cast<const float*>(ds.p), dout.p, (int)M, (int)N,
@@ -322,11 +370,10 @@ int run_fp8sim(int argc, char** argv) {
   const std::string fmt = argv[2];
   if (fmt != "e4m3" && fmt != "e5m2") return usage("fp8sim: format must be e4m3 or e5m2");
   Npy a = read_npy(argv[3], "<V2"), w = read_npy(argv[4], "<V2");
-  const int64_t K = a.shape.back(), M = a.size() / K, N = w.shape[1];
-  if (w.shape[0] != K) {
-    std::fprintf(stderr, "fp8sim: contraction mismatch\n");
-    return 1;
-  }
+  int64_t M = 0, K = 0;
+  if (!rows_cols(a, M, K)) return shape_error("fp8sim", "A " + dims_str(a));
+  if (!is_kn(w, K)) return shape_error("fp8sim", "W " + dims_str(w) + " is not [K, N]");
+  const int64_t N = w.shape[1];
   std::fprintf(stderr, "[pkb200-cuda_run] path=fp8_sim fmt=%s M=%lld N=%lld K=%lld\n",
                fmt.c_str(), (long long)M, (long long)N, (long long)K);
   Dev da(a), dw(w), dout(static_cast<size_t>(M * N) * 2);
@@ -344,7 +391,15 @@ int run_mlp_block(int argc, char** argv) {
   if (!o.ok) return usage(u);
   Npy x = read_npy(argv[2], "<V2"), g = read_npy(argv[3], "<V2"), w1 = read_npy(argv[4], "<V2"),
       b1 = read_npy(argv[5], "<V2"), w2 = read_npy(argv[6], "<V2"), b2 = read_npy(argv[7], "<V2");
-  const int64_t d = x.shape.back(), M = x.size() / d, ffn = w1.shape[1];
+  int64_t M = 0, d = 0;
+  if (!rows_cols(x, M, d)) return shape_error("mlp_block", "X " + dims_str(x));
+  if (!is_vec(g, d)) return shape_error("mlp_block", "GAMMA " + dims_str(g) + " != d");
+  if (!is_kn(w1, d)) return shape_error("mlp_block", "W1 " + dims_str(w1) + " is not [d, ffn]");
+  const int64_t ffn = w1.shape[1];
+  if (!is_vec(b1, ffn)) return shape_error("mlp_block", "B1 " + dims_str(b1) + " != ffn");
+  if (!is_kn(w2, ffn) || w2.shape[1] != d)
+    return shape_error("mlp_block", "W2 " + dims_str(w2) + " is not [ffn, d]");
+  if (!is_vec(b2, d)) return shape_error("mlp_block", "B2 " + dims_str(b2) + " != d");
   Dev dx(x), dg(g), dw1(w1), db1(b1), dw2(w2), db2(b2), dy(x.bytes.size());
   const size_t wsb = pkb200_mlp_block_workspace_size((int)M, (int)d, (int)ffn);
   Dev ws(wsb);
@@ -361,7 +416,10 @@ int run_attention_prefill(int argc, char** argv) {
   Opts o = parse_opts(argc, argv, 6);
   if (!o.ok) return usage(u);
   Npy q = read_npy(argv[2], "<V2"), k = read_npy(argv[3], "<V2"), v = read_npy(argv[4], "<V2");
-  if (q.shape.size() != 4 || k.shape.size() != 4 || v.shape != k.shape) return usage(u);
+  if (!is_4d(q) || !is_4d(k) || v.shape != k.shape)
+    return shape_error("attention_prefill", "Q " + dims_str(q) + " K " + dims_str(k) + " V " + dims_str(v));
+  if (k.shape[0] != q.shape[0] || k.shape[1] != q.shape[1] || k.shape[3] != q.shape[3])
+    return shape_error("attention_prefill", "K " + dims_str(k) + " does not match Q " + dims_str(q) + " in B, H or D");
   const int B = (int)q.shape[0], H = (int)q.shape[1], Sq = (int)q.shape[2], D = (int)q.shape[3];
   const int Skv = (int)k.shape[2];
   const float scale = std::isnan(o.scale) ? 1.0f / std::sqrt(static_cast<float>(D)) : o.scale;
@@ -376,7 +434,9 @@ int run_attention_prefill(int argc, char** argv) {
 int run_kv_cache_update(int argc, char** argv) {
   if (argc != 5) return usage("kv_cache_update CACHE NEW OUT");
   Npy c = read_npy(argv[2], "<V2"), n = read_npy(argv[3], "<V2");
-  if (c.shape.size() != 4 || n.shape.size() != 4) return usage("kv_cache_update CACHE NEW OUT");
+  if (!is_4d(c) || !is_4d(n) || n.shape[0] != c.shape[0] || n.shape[1] != c.shape[1] ||
+      n.shape[3] != c.shape[3])
+    return shape_error("kv_cache_update", "CACHE " + dims_str(c) + " NEW " + dims_str(n));
   const int B = (int)c.shape[0], H = (int)c.shape[1], Sc = (int)c.shape[2], D = (int)c.shape[3];
   const int Sn = (int)n.shape[2];
   Dev dc(c), dn(n), dout(static_cast<size_t>(B) * H * (Sc + Sn) * D * 2);
@@ -396,6 +456,13 @@ int run_attention_append(int argc, char** argv) {
   if (!o.ok) return usage(u);
   Npy q = read_npy(argv[2], "<V2"), kn = read_npy(argv[3], "<V2"), vn = read_npy(argv[4], "<V2"),
       kc = read_npy(argv[5], "<V2"), vc = read_npy(argv[6], "<V2");
+  if (!is_4d(q) || kn.shape != q.shape || vn.shape != q.shape)
+    return shape_error("attention_append", "Q " + dims_str(q) + " KNEW " + dims_str(kn) + " VNEW " + dims_str(vn));
+  if (!is_4d(kc) || vc.shape != kc.shape || kc.shape[0] != q.shape[0] || kc.shape[1] != q.shape[1] ||
+      kc.shape[3] != q.shape[3])
+    return shape_error("attention_append", "KCACHE " + dims_str(kc) + " VCACHE " + dims_str(vc));
+  if (o.s_cache < 0 || o.s_cache + q.shape[2] > kc.shape[2])
+    return shape_error("attention_append", "s_cache + S_new exceeds the cache rows");
   const int B = (int)q.shape[0], H = (int)q.shape[1], Sq = (int)q.shape[2], D = (int)q.shape[3];
   const int Smax = (int)kc.shape[2];
   Dev dq(q), dkn(kn), dvn(vn), dkc(kc), dvc(vc), dout(q.bytes.size());

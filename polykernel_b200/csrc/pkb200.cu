@@ -15,6 +15,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <set>
 #include <utility>
 
 #include "attention_tc.cuh"
@@ -217,10 +218,33 @@ tuning::Config select_config(int epi, int M, int N, int K, int* source = nullptr
 }
 
 // -------------------------------------------------------------------- GEMM --
+// One-time per-device initialisation (kernel attributes, symbol addresses) is
+// guarded by its own mutex, so entry points called from several host threads
+// at once stay safe.
+std::mutex g_init_mu;
+
+// Opts `func` into `smem` bytes of dynamic shared memory on the current device
+// (once per (kernel, device)).
+int ensure_smem_attr(const void* func, int smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  static std::set<std::pair<const void*, int>> done;
+  if (done.count({func, dev})) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  done.insert({func, dev});
+  return cudaSuccess;
+}
+
 // Tile counters of the dynamic GEMM schedule: one per launch, taken round
-// robin and zeroed in stream order before the launch (launches in flight at
-// the same time on different streams get different counters).
-constexpr int kNumTileCounters = 256;
+// robin and zeroed in stream order before the launch, so launches in flight
+// at the same time on different streams get different counters. At most
+// kNumTileCounters dynamic-schedule GEMM launches may be in flight (enqueued
+// and not yet finished) at once on one device; beyond that a counter would be
+// shared by two running launches.
+constexpr int kNumTileCounters = 4096;
 __device__ int g_tile_counters[kNumTileCounters];
 std::atomic<int> g_gemm_dynamic{1};
 std::atomic<unsigned> g_tile_counter_next{0};
@@ -228,11 +252,14 @@ std::atomic<unsigned> g_tile_counter_next{0};
 int next_tile_counter(int dev, int** out) {
   static int* base[kMaxDevices] = {};
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!base[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_tile_counters);
-    if (e != cudaSuccess) return e;
-    base[dev] = static_cast<int*>(p);
+  {
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (!base[dev]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_tile_counters);
+      if (e != cudaSuccess) return e;
+      base[dev] = static_cast<int*>(p);
+    }
   }
   *out = base[dev] + (g_tile_counter_next.fetch_add(1) % kNumTileCounters);
   return cudaSuccess;
@@ -244,15 +271,10 @@ int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, i
                         const PeerMaps* peer = nullptr) {
   constexpr int smem = EPI == kEpiPeerStoreF32 ? gemm::smem_bytes_peer(BN, STAGES)
                                                : gemm::smem_bytes(BN, STAGES);
-  static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, BN, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  if (const int e = ensure_smem_attr(reinterpret_cast<const void*>(gemm_tc_kernel<EPI, BN, STAGES>), smem))
+    return e;
   const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + BN - 1) / BN);
   int ctas = di->sms;
   const int cap = g_gemm_max_ctas.load();
@@ -469,16 +491,9 @@ int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, i
     mks = mka;
     mvs = mva;
   }
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  if (const int e = ensure_smem_attr(reinterpret_cast<const void*>(attention_tc_kernel<D>),
+                                     L::SMEM_BYTES))
+    return e;
   AttnTcParams p{};
   p.BH = BH;
   p.S_q = S_q;
@@ -701,6 +716,7 @@ struct TpCePlan {
   cudaEvent_t ev_gemm[kMaxTpChunks] = {}, ev_end[2 * kMaxPeers + 1] = {}, ev_step = nullptr,
               ev_done = nullptr;
   unsigned last_epoch = 0;
+  int joined_streams = 0;                 // exchange streams joined into the caller's by the last step
   bool aborted = false;
   cudaStream_t push_for(int p) const { return push[nstreams == 1 ? 0 : p]; }
   cudaStream_t pull_for(int p) const { return pull[nstreams == 1 ? 0 : p]; }
@@ -793,17 +809,23 @@ int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const
     }
   }
   // the caller's stream continues once every copy and the last reduce are done
+  // One join event per push/pull stream used (k counts them) plus the reduce
+  // stream's; every peer's streams are joined when each peer has its own.
   int k = 0;
-  for (int k = 1; k < W; ++k) {
-    const int p = (me + k) % W;
-    if (pl->nstreams == 1 && k != 1) continue;
+  for (int jp = 1; jp < W; ++jp) {
+    const int p = (me + jp) % W;
+    if (pl->nstreams == 1 && jp != 1) continue;
     for (cudaStream_t s : {pl->push_for(p), pl->pull_for(p)}) {
       if ((e = ck(cudaEventRecord(pl->ev_end[k], s)))) return e;
-      if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k++], 0)))) return e;
+      if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k], 0)))) return e;
+      ++k;
     }
   }
   if ((e = ck(cudaEventRecord(pl->ev_end[k], pl->red)))) return e;
   if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k], 0)))) return e;
+  pl->joined_streams = k + 1;
+  // every push and pull stream (one pair per peer, or one pair) plus the reduce stream
+  if (pl->joined_streams != 2 * (pl->nstreams == 1 ? 1 : W - 1) + 1) return cudaErrorUnknown;
   pl->last_epoch = epoch;
   return ck(cudaEventRecord(pl->ev_done, main));
 }
@@ -1037,6 +1059,13 @@ int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_sha
   // streams that no peer will satisfy: the plan is not reused
   if (e) pl->aborted = true;
   return e;
+}
+
+int pkb200_tp_ce_joined_streams(void* plan, int* count) {
+  auto* pl = static_cast<TpCePlan*>(plan);
+  if (!pl || !count) return cudaErrorInvalidValue;
+  *count = pl->joined_streams;
+  return cudaSuccess;
 }
 
 int pkb200_tp_ce_wait(void* plan, int timeout_ms) {

@@ -14,8 +14,8 @@ the fp32 partials, epilogue on this rank's rows, all-gather of the bf16
 result) overlaps GEMM2 of the next chunk. Three exchanges implement it:
 
 * "copy_engine" (pkb200_tp_ce_*): the copy engines push each partial row block
-  into its owner's slot buffer (torch symmetric memory) with an epoch flag
-  behind it; the owner waits on the flags with stream memory operations, sums
+  into its owner's slot buffer (plain device memory mapped into every peer with
+  CUDA IPC handles) with an epoch flag behind it; the owner waits on the flags with stream memory operations, sums
   the slots and publishes its rows, which the peers' copy engines pull. No SM
   is spent on data movement, so the persistent GEMM keeps every SM.
 * "nccl": NCCL reduce-scatter + all-gather on a side stream.
@@ -23,6 +23,8 @@ result) overlaps GEMM2 of the next chunk. Three exchanges implement it:
   owners' slot buffers over NVLink (pkb200_matmul_peer_store_f32).
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -261,6 +263,15 @@ class TensorParallelMLP:
                                           self._epoch, torch.cuda.current_stream().cuda_stream),
               "tp_ce_mlp_step")
         return out
+
+    def joined_streams(self):
+        """Exchange streams the last copy-engine step joined back into the
+        caller's stream (2*(world-1)+1 with per-peer streams, else 3)."""
+        from ._lib import check, lib
+        n = ctypes.c_int(0)
+        check(lib().pkb200_tp_ce_joined_streams(self._ce["plan"], ctypes.byref(n)),
+              "tp_ce_joined_streams")
+        return int(n.value)
 
     def wait(self, timeout_ms=None):
         """Host wait for the last copy-engine step with a deadline; raises

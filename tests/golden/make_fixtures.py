@@ -24,8 +24,16 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None,
+                    help="reference checkout (default: $PK_REFERENCE, else BASELINE.json's "
+                         "reference_path)")
     args = ap.parse_args()
+    if args.ref is None:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+        from __graft_entry__ import reference_checkout
+        args.ref = reference_checkout()
+        if args.ref is None:
+            raise SystemExit("reference checkout not found: pass --ref or set PK_REFERENCE")
     sys.path.insert(0, os.path.join(args.ref, "tests", "golden"))
     import ml_dtypes  # noqa: F401
     import golden as G  # the reference golden

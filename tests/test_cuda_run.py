@@ -48,6 +48,76 @@ def test_missing_input_is_runtime_error(tmp_path):
     assert r.returncode == 1 and "cannot open" in r.stderr
 
 
+def _bf(tmp_path, name, shape):
+    path = tmp_path / f"{name}.npy"
+    _save(path, np.zeros(shape, np.uint16))
+    return path
+
+
+def _bf0d(tmp_path, name):
+    path = tmp_path / f"{name}.npy"
+    np.save(path, np.zeros((), np.uint16).view("V2"))
+    return path
+
+
+def _i8(tmp_path, name, shape):
+    path = tmp_path / f"{name}.npy"
+    np.save(path, np.zeros(shape, np.int8))
+    return path
+
+
+def _f4(tmp_path, name, shape):
+    path = tmp_path / f"{name}.npy"
+    np.save(path, np.zeros(shape, np.float32))
+    return path
+
+
+@pytest.mark.parametrize("case", [
+    "matmul_k", "matmul_rank", "matmul_0d", "frm_gamma", "fbg_bias", "int8_scale", "rmsnorm_w",
+    "mlp_w1", "mlp_b1", "mlp_w2", "mlp_gamma", "attn_bhd", "attn_v", "kv_d", "append_cache",
+    "append_scache", "fp8_k"])
+def test_mismatched_shapes_rejected_before_device_work(tmp_path, case):
+    """Every operand is checked against the primary one before any device
+    allocation: a mismatched file exits 1 with a shape error (no GPU needed)."""
+    t = tmp_path
+    out = t / "out.npy"
+    a = _bf(t, "a", (8, 16))
+    args = {
+        "matmul_k": lambda: ("matmul", a, _bf(t, "b", (15, 4)), out),
+        "matmul_rank": lambda: ("matmul", a, _bf(t, "b", (16,)), out),
+        "matmul_0d": lambda: ("matmul", _bf0d(t, "z"), _bf(t, "b", (1, 4)), out),
+        "frm_gamma": lambda: ("fused_rmsnorm_matmul", a, _bf(t, "b", (16, 4)), out, "--weight",
+                      _bf(t, "g", (15,))),
+        "fbg_bias": lambda: ("fused_matmul_bias_gelu", a, _bf(t, "b", (16, 4)), _bf(t, "bias", (5,)), out),
+        "int8_scale": lambda: ("matmul_int8", a, _i8(t, "wq", (16, 4)), _f4(t, "s", (3,)), out),
+        "rmsnorm_w": lambda: ("rmsnorm", a, out, "--weight", _bf(t, "w", (8,))),
+        "mlp_w1": lambda: ("mlp_block", a, _bf(t, "g", (16,)), _bf(t, "w1", (8, 32)), _bf(t, "b1", (32,)),
+                   _bf(t, "w2", (32, 16)), _bf(t, "b2", (16,)), out),
+        "mlp_b1": lambda: ("mlp_block", a, _bf(t, "g", (16,)), _bf(t, "w1", (16, 32)), _bf(t, "b1", (31,)),
+                   _bf(t, "w2", (32, 16)), _bf(t, "b2", (16,)), out),
+        "mlp_w2": lambda: ("mlp_block", a, _bf(t, "g", (16,)), _bf(t, "w1", (16, 32)), _bf(t, "b1", (32,)),
+                   _bf(t, "w2", (32, 8)), _bf(t, "b2", (16,)), out),
+        "mlp_gamma": lambda: ("mlp_block", a, _bf(t, "g", (17,)), _bf(t, "w1", (16, 32)),
+                      _bf(t, "b1", (32,)), _bf(t, "w2", (32, 16)), _bf(t, "b2", (16,)), out),
+        "attn_bhd": lambda: ("attention_prefill", _bf(t, "q", (1, 2, 8, 32)), _bf(t, "k", (1, 3, 8, 32)),
+                     _bf(t, "v", (1, 3, 8, 32)), out),
+        "attn_v": lambda: ("attention_prefill", _bf(t, "q", (1, 2, 8, 32)), _bf(t, "k", (1, 2, 8, 32)),
+                   _bf(t, "v", (1, 2, 7, 32)), out),
+        "kv_d": lambda: ("kv_cache_update", _bf(t, "c", (1, 2, 8, 32)), _bf(t, "n", (1, 2, 4, 16)), out),
+        "append_cache": lambda: ("attention_append", _bf(t, "q", (1, 2, 8, 32)), _bf(t, "kn", (1, 2, 8, 32)),
+                         _bf(t, "vn", (1, 2, 8, 32)), _bf(t, "kc", (1, 2, 16, 64)),
+                         _bf(t, "vc", (1, 2, 16, 64)), out, t / "ko.npy", t / "vo.npy"),
+        "append_scache": lambda: ("attention_append", _bf(t, "q", (1, 2, 8, 32)), _bf(t, "kn", (1, 2, 8, 32)),
+                          _bf(t, "vn", (1, 2, 8, 32)), _bf(t, "kc", (1, 2, 16, 32)),
+                          _bf(t, "vc", (1, 2, 16, 32)), out, t / "ko.npy", t / "vo.npy",
+                          "--s-cache", "9"),
+        "fp8_k": lambda: ("fp8sim", "e4m3", a, _bf(t, "w", (12, 4)), out),
+    }[case]()
+    r = _run(*args)
+    assert r.returncode == 1 and "shape error" in r.stderr, (r.returncode, r.stderr)
+    assert not out.exists()
+
+
 @pytest.mark.gpu
 def test_dev_and_neg(cuda):
     r = _run("dev")

@@ -14,16 +14,16 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _two_gpus():
+def _gpus():
     import torch
-    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _run(mode, port):
-    if not _two_gpus():
-        pytest.skip("needs 2 GPUs")
+def _run(mode, port, nproc=2):
+    if _gpus() < nproc:
+        pytest.skip(f"needs {nproc} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", CUDA_DEVICE_MAX_CONNECTIONS="32")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", str(nproc),
            "--master-addr", "127.0.0.1", "--master-port", str(port),
            os.path.join(ROOT, "tests", "tp_worker.py"), mode]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
@@ -32,13 +32,18 @@ def _run(mode, port):
     return json.loads(lines[-1][len("RESULT "):])
 
 
-def test_tp_exchanges_match_single_gpu():
-    res = _run("parity", 29711)
+@pytest.mark.parametrize("nproc", [2, 4])
+def test_tp_exchanges_match_single_gpu(nproc):
+    res = _run("parity", 29711 + nproc, nproc)
     print(res)
     for name in ("copy_engine", "copy_engine_one_stream", "nccl", "peer_store"):
         # the only change from one GPU is the fp32 summation order of the partials
         assert res[name]["bit_exact"] >= 0.93, (name, res[name])
         assert res[name]["max_err_over_scale"] <= 2.0 ** -6, (name, res[name])
+        # each rank's row block arrives (own reduce and every peer's pulled rows)
+        assert min(res[name + "_blocks_exact"]) >= 0.9, (name, res[name + "_blocks_exact"])
+    assert res["copy_engine_joined_streams"] == 2 * (nproc - 1) + 1
+    assert res["copy_engine_one_stream_joined_streams"] == 3
     assert res["ranks_agree"]
     assert res["ce_eq_one_stream"] and res["ce_eq_peer_store"]
     assert res["device_error"] == 0

@@ -117,7 +117,7 @@ def test_int8_matches_quant_golden(golden):
 @pytest.fixture(scope="module")
 def reflib():
     if not os.path.exists(REF_LIB):
-        pytest.skip("oracle/_ref not built (make -C oracle)")
+        pytest.skip("oracle/_ref not built (built by __graft_entry__.build())")
     lib = ctypes.CDLL(REF_LIB)
     return lib
 
@@ -223,7 +223,7 @@ def test_reference_cpu_fp8_rounding_matches_oracle(tmp_path, fmt):
     import subprocess
     exe = os.path.join(os.path.dirname(REF_LIB), "matmul_quant")
     if not os.path.exists(exe):
-        pytest.skip("oracle/_ref not built (make -C oracle)")
+        pytest.skip("oracle/_ref not built (built by __graft_entry__.build())")
     w = fp8_edge_weights(fmt).reshape(4, 8)
     eye = np.eye(4, dtype=np.float32)
     np.save(tmp_path / "a.npy", O.to_bits(eye).view("V2"))

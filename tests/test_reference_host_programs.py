@@ -24,7 +24,7 @@ F = O.from_bits
 
 def _need(path):
     if not os.path.exists(path):
-        pytest.skip(f"{os.path.relpath(path, ROOT)} not built (make -C oracle)")
+        pytest.skip(f"{os.path.relpath(path, ROOT)} not built (built by __graft_entry__.build())")
     return path
 
 

@@ -96,10 +96,13 @@ def test_shard_range_rejects_uneven():
         shard_range(10, 0, 3)
 
 
-def test_tp_bench_cli_help():
-    """The TP exchange benchmark's command line parses without a GPU."""
+def test_bench_cli_help():
+    """bench.py's command line (the TP exchange breakdown and the profiling
+    cases included) parses without a GPU."""
+    import os
     import subprocess
     import sys
-    r = subprocess.run([sys.executable, "-m", "polykernel_b200.tp_bench", "--help"],
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--help"],
                        capture_output=True, text=True, timeout=120)
-    assert r.returncode == 0 and "--chunks" in r.stdout
+    assert r.returncode == 0 and "--tp-breakdown" in r.stdout and "--profile-case" in r.stdout

@@ -58,6 +58,13 @@ def parity(rank, world, host):
             y = m(X2)
         m.wait(10000) if name.startswith("copy_engine") else torch.cuda.synchronize()
         outs[name] = y
+        if name.startswith("copy_engine"):
+            res[name + "_joined_streams"] = m.joined_streams()
+        # every rank's row block (the owner's reduce + the pulls), separately
+        per = M // world
+        res[name + "_blocks_exact"] = [
+            (y[p * per:(p + 1) * per] == ref[p * per:(p + 1) * per]).float().mean().item()
+            for p in range(world)]
         ex = (y == ref).float().mean().item()
         rel = ((y.float() - ref.float()).abs() / ref.float().abs().clamp_min(
             ref.float().pow(2).mean().sqrt())).max().item()
