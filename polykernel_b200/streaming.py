@@ -1,5 +1,10 @@
 """Host-resident inputs and outputs with copies overlapped against compute.
 
+Two forms: `HostStreamed` streams row chunks of one row-independent call (the
+MLP block) through two device buffers; `HostStepPipeline` overlaps whole
+steps (all of a step's inputs and outputs) with the neighbouring steps'
+compute through two device buffer sets.
+
 `HostStreamed(forward, chunks)` runs `forward(x, out)` (a device function that
 writes the [rows, d_out] result for a [rows, d] bf16 input into `out`; it must be
 row-independent, as the MLP block is) over row chunks of a pinned host tensor: the host->device copy of chunk
@@ -99,3 +104,70 @@ class HostStreamed:
     def copy_streams(self):
         """(host->device, device->host) streams, for callers that queue more copies."""
         return (self._bufs[3], self._bufs[4]) if self._bufs else (None, None)
+
+
+class HostStepPipeline:
+    """Steps over host-resident inputs and outputs with the copies of
+    neighbouring steps overlapped against compute.
+
+    `host_inputs` / `host_outputs` are pinned host tensors. Each `step(compute)`
+    copies the inputs into one of `depth` device buffer sets on a copy stream,
+    runs `compute(device_inputs, device_outputs)` on the current stream, and
+    copies the outputs back on a second copy stream. A buffer set is reused
+    only after its previous device->host copy finished, so step i+1's inputs
+    cross PCIe while step i computes and step i-1's outputs drain: end-to-end
+    time approaches max(compute, H2D, D2H) per step. `wait(stream)` makes a
+    stream wait for every copy queued so far. The host input tensors must not
+    be rewritten until the step that reads them has been joined."""
+
+    def __init__(self, host_inputs, host_outputs, device="cuda", depth=2):
+        self.device = torch.device(device)
+        self.hin = list(host_inputs)
+        self.hout = list(host_outputs)
+        self.depth = max(1, int(depth))
+        self.din = [[torch.empty(h.shape, dtype=h.dtype, device=self.device) for h in self.hin]
+                    for _ in range(self.depth)]
+        self.dout = [[torch.empty(h.shape, dtype=h.dtype, device=self.device) for h in self.hout]
+                     for _ in range(self.depth)]
+        self.s_in = torch.cuda.Stream(self.device)
+        self.s_out = torch.cuda.Stream(self.device)
+        self._free = [None] * self.depth   # set k's last device->host copy done
+        self._i = 0
+
+    @property
+    def h2d_bytes(self):
+        return sum(h.numel() * h.element_size() for h in self.hin)
+
+    @property
+    def d2h_bytes(self):
+        return sum(h.numel() * h.element_size() for h in self.hout)
+
+    def step(self, compute):
+        k = self._i % self.depth
+        self._i += 1
+        comp = torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(self.s_in):
+            if self._free[k] is not None:
+                self.s_in.wait_event(self._free[k])    # set k's previous step fully drained
+            for h, d in zip(self.hin, self.din[k]):
+                d.copy_(h, non_blocking=True)
+            copied = torch.cuda.Event()
+            copied.record(self.s_in)
+        comp.wait_event(copied)
+        compute(self.din[k], self.dout[k])
+        done = torch.cuda.Event()
+        done.record(comp)
+        with torch.cuda.stream(self.s_out):
+            self.s_out.wait_event(done)
+            for h, d in zip(self.hout, self.dout[k]):
+                h.copy_(d, non_blocking=True)
+            drained = torch.cuda.Event()
+            drained.record(self.s_out)
+        self._free[k] = drained
+        return self.dout[k]
+
+    def wait(self, stream=None):
+        stream = stream or torch.cuda.current_stream(self.device)
+        for e in self._free:
+            if e is not None:
+                stream.wait_event(e)

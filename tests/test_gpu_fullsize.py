@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 from oracle import golden_np as O
-from tests.helpers import check_attention, check_chain, f32_from_t
+from tests.helpers import bits_from_t, check_attention, check_chain, f32_from_t
 
 pytestmark = pytest.mark.gpu
 
@@ -107,3 +107,60 @@ def test_gemm_bit_identical_to_cublas(cuda, shape):
     rows = np.sort(np.random.default_rng(1).choice(M, 8, replace=False))
     gold = O.matmul(f32_from_t(a[rows]), f32_from_t(b))
     print(shape, check_chain(f32_from_t(ours[rows]), gold, min_exact=0.98))
+
+
+# ------------------------------------------ the reference arm's exact inputs --
+# bench.py's seeded NumPy draws (numpy.random.default_rng; fixed draw order per
+# config), the same arrays the reference-CPU arm of bench.py consumes.
+def _dev_bits(bits):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(bits).astype(np.int16)).view(torch.bfloat16).cuda()
+
+
+@pytest.mark.parametrize("cfg", [(2048, 4096, 16384), (16384, 8192, 28672)],
+                         ids=["config2", "config5"])
+def test_mlp_block_full_size_on_reference_arm_inputs(cuda, cfg):
+    import bench
+    import polykernel_b200 as pk
+    M, d, ffn = cfg
+    host = bench.synthetic_host_weights(M, d, ffn, seed=0)
+    y = pk.ops.mlp_block(*(_dev_bits(a) for a in host), eps=1e-6)
+    rows = np.sort(np.random.default_rng(1).choice(M, 8, replace=False))
+    x, gamma, w1, b1, w2, b2 = (O.from_bits(a) for a in host)
+    ref = O.mlp_block(x[rows], gamma, w1, b1, w2, b2, eps=1e-6)
+    print(cfg, check_chain(f32_from_t(y[rows]), ref))
+    assert pk.device_error() == 0
+
+
+def test_int8_mlp_full_size_on_seeded_inputs(cuda):
+    import torch
+    import bench
+    import polykernel_b200 as pk
+    M, d, ffn = 4096, 4096, 14336
+    x, gamma, q1, s1, b1, q2, s2, b2 = bench.synthetic_host_int8(M, d, ffn, seed=0)
+    dq = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    y = pk.ops.mlp_block_int8(_dev_bits(x), _dev_bits(gamma), dq(q1), dq(s1), _dev_bits(b1),
+                              dq(q2), dq(s2), _dev_bits(b2), eps=1e-6)
+    rows = np.sort(np.random.default_rng(2).choice(M, 8, replace=False))
+    ref = O.mlp_block_int8(O.from_bits(x)[rows], O.from_bits(gamma), q1, s1, O.from_bits(b1),
+                           q2, s2, O.from_bits(b2), eps=1e-6)
+    print("config4", check_chain(f32_from_t(y[rows]), ref))
+
+
+def test_attention_full_size_on_reference_arm_inputs(cuda):
+    import torch
+    import bench
+    import polykernel_b200 as pk
+    B, H, S, D, S_max = 4, 32, 2048, 128, 4096
+    q, k, v = bench.synthetic_host_attention(B, H, S, D, seed=1)
+    kc = torch.zeros(B, H, S_max, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    o = pk.ops.attention_prefill_kv_append(_dev_bits(q), _dev_bits(k), _dev_bits(v), kc, vc, 0,
+                                           causal=True)
+    assert np.array_equal(bits_from_t(kc[:, :, :S]), k) and np.array_equal(bits_from_t(vc[:, :, :S]), v)
+    for (b, h) in ((0, 0), (0, 1), (3, 31)):        # (0,0), (0,1): heads the reference arm times
+        qf, kf, vf = (O.from_bits(a[b:b + 1, h:h + 1]) for a in (q, k, v))
+        ref = O.attention_prefill(qf, kf, vf, causal=True)
+        ref64 = O.attention_prefill(qf, kf, vf, causal=True, acc=np.float64)
+        print((b, h), check_attention(f32_from_t(o[b:b + 1, h:h + 1]), ref, s_kv=S, ref64_f32=ref64))
+    assert pk.device_error() == 0
