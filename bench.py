@@ -372,17 +372,24 @@ def run_gpu_arm(args):
         launches_per_step = 3 + 1
     else:
         if args.tp_mode == "auto":
-            # measured: the copy-engine exchange is faster at 2 ranks (2381 vs
-            # 2137 TFLOP/s), NCCL at 8 (4994 vs 4508); 4 ranks keep NCCL
-            args.tp_mode = "ce" if world == 2 else "nccl"
+            # measured whole-job TFLOP/s: the copy-engine exchange wins at every
+            # N (N=4: 4063 vs 3534 with NCCL; N=8 with GEMM1 in row chunks too:
+            # 5290 vs 4826 with NCCL and 4498 with GEMM1 unchunked)
+            args.tp_mode = "ce"
+            if world >= 8:
+                args.tp_gemm1_chunked = True
         reduce = {"fused": "peer_store", "nccl": "nccl", "ce": "copy_engine"}[args.tp_mode]
         tpm = TensorParallelMLP(gamma, w1, b1, w2, b2, eps, chunks=args.tp_chunks, reduce=reduce,
-                                per_peer_streams=not args.tp_one_stream)
+                                per_peer_streams=not args.tp_one_stream,
+                                gemm1_chunked=args.tp_gemm1_chunked)
 
         def mlp(xx, out):
             return tpm(xx, out=out)
-        launches_per_step = {"fused": 2 + 2 + 1, "nccl": 2 + 2 * args.tp_chunks + 1,
-                             "ce": 2 + 2 * args.tp_chunks}[args.tp_mode]
+        # rmsnorm, GEMM1 (per chunk when chunked), GEMM2 per chunk, the
+        # reduce/epilogue kernel per chunk, attention
+        C = args.tp_chunks
+        launches_per_step = {"fused": 2 + 2 + 1, "nccl": 3 + 2 * C,
+                             "ce": (2 + 3 * C) if args.tp_gemm1_chunked else (3 + 2 * C)}[args.tp_mode]
 
     stream = torch.cuda.current_stream()
     # events around the dominant kernel (GEMM1 with the bias+GELU epilogue) are
@@ -465,7 +472,9 @@ def run_gpu_arm(args):
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, kn, vn))
     yh = torch.empty(r_hi - r_lo, d, dtype=bf).pin_memory()
     oh = torch.empty_like(o, device="cpu").pin_memory()
-    pipe = HostStepPipeline([xh, qh, kh, vh], [yh, oh], dev)
+    # three buffer sets: step i+1's host->device copies need not wait for step
+    # i-1's device->host copies, so both directions of the host link run at once
+    pipe = HostStepPipeline([xh, qh, kh, vh], [yh, oh], dev, depth=3)
     if world > 1:
         xg = torch.empty(M, d, dtype=bf, device=dev)
         yg = torch.empty(M, d, dtype=bf, device=dev)
@@ -503,6 +512,19 @@ def run_gpu_arm(args):
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     h2d, d2h = pipe.h2d_bytes, pipe.d2h_bytes
+    # Breakdown: the same pipeline with no compute (copies only, every rank at
+    # once, so a shared host link shows), against the device step and the
+    # overlapped end-to-end step above.
+    barrier()
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for _ in range(args.steps):
+        pipe.step(lambda din, dout: None)
+    pipe.wait(stream)
+    c1.record(stream)
+    barrier()
+    copy_only_ms = c0.elapsed_time(c1) / args.steps
     del pipe
 
     # Parity of the timed step, on every run and every N: 8 sampled token rows
@@ -562,6 +584,7 @@ def run_gpu_arm(args):
         return float(t.item())
 
     ms, gemm1_ms, attn_ms, e2e_ms = gmax(ms), gmax(gemm1_ms), gmax(attn_ms), gmax(e2e_ms)
+    copy_only_ms = gmax(copy_only_ms)
     attn_after_mlp_ms = gmax(attn_after_mlp_ms)
     err = pk.device_error()
 
@@ -653,7 +676,8 @@ def run_gpu_arm(args):
                        "mlp": {"M": M, "d": d, "ffn": ffn}, "attention":
                        {"B": B, "H": H, "S": S, "D": D, "S_cache": 0, "cache_rows": S_max},
                        "parallelism": f"tp{world} (MLP) / heads{world} (attention)",
-                       "tp_exchange": args.tp_mode if world > 1 else None,
+                       "tp_exchange": (args.tp_mode + ("+gemm1_chunked" if args.tp_gemm1_chunked
+                                                       else "")) if world > 1 else None,
                        "l2": "inputs larger than L2 (no flush needed)"},
             "parts": {"mlp_tflops": mlp_flops(M, d, ffn) / ((ms - attn_after_mlp_ms) * 1e-3) / 1e12,
                       "attention_ms": attn_ms, "attention_tflops_whole_job": a_tflops * world,
@@ -670,7 +694,12 @@ def run_gpu_arm(args):
             "cpu_baseline": cpu,
             "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "bytes_scope": "per rank", "rows_bit_exact_vs_device_step": e2e_rows_exact},
+                    "bytes_scope": "per rank", "rows_bit_exact_vs_device_step": e2e_rows_exact,
+                    "breakdown_ms": {"copy_only": copy_only_ms, "compute_only": ms,
+                                     "overlapped": e2e_ms},
+                    "host_link_gbs_all_ranks": {
+                        "h2d": world * h2d / (copy_only_ms * 1e-3) / 1e9,
+                        "d2h": world * d2h / (copy_only_ms * 1e-3) / 1e9}},
             "gpu_launches": launches_per_step * args.steps,
             "other_configs": others,
             "other_configs_timed": "each alone after 2 s idle (burst clocks)" if others else None,
@@ -856,12 +885,22 @@ def run_tp_breakdown(args):
         streams = [torch.cuda.Stream(dev) for _ in range(world)]
         peers = [(rank + k) % world for k in range(1, world)]
 
-        def copies(push, pull, per_peer):
+        wstreams = [torch.cuda.Stream(dev) for _ in range(world)]
+
+        def copies(push, pull, per_peer, write_rows=False):
             ev = torch.cuda.Event()
             ev.record(main_s)
             for p in peers:
                 s = streams[p if per_peer else 0]
                 s.wait_event(ev)
+                if write_rows:
+                    # the owner writes its bf16 rows into the peer (a write, on
+                    # its own stream beside the partial pushes)
+                    ws = wstreams[p if per_peer else 0]
+                    ws.wait_event(ev)
+                    check(lib().pkb200_copy_async(
+                        rows16.ptrs[p], mine16.data_ptr(), per * d * 2, ws.cuda_stream),
+                        "copy_async")
                 if push:
                     check(lib().pkb200_copy_async(
                         slots.ptrs[p] + rank * per * d * 4, y32[p * per:(p + 1) * per].data_ptr(),
@@ -872,8 +911,16 @@ def run_tp_breakdown(args):
                         s.cuda_stream), "copy_async")
             for s in (streams if per_peer else streams[:1]):
                 main_s.wait_stream(s)
+            if write_rows:
+                for s in (wstreams if per_peer else wstreams[:1]):
+                    main_s.wait_stream(s)
 
         for mode, per_peer in (("per_peer", True), ("one_stream", False)):
+            emit("ce_push_rows_write", _tp_time(lambda: copies(False, False, per_peer, True),
+                                                args.iters, args.warmup, dev), pull_bytes,
+                 streams=mode)
+            emit("ce_push_push", _tp_time(lambda: copies(True, False, per_peer, True), args.iters,
+                                          args.warmup, dev), push_bytes + pull_bytes, streams=mode)
             emit("ce_push", _tp_time(lambda: copies(True, False, per_peer), args.iters,
                                   args.warmup, dev), push_bytes, streams=mode)
             emit("ce_pull", _tp_time(lambda: copies(False, True, per_peer), args.iters,
@@ -919,6 +966,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="pkb200", choices=["pkb200", "reference"])
     ap.add_argument("--tp-chunks", type=int, default=4)
+    ap.add_argument("--tp-gemm1-chunked", action="store_true",
+                    help="copy-engine exchange: run GEMM1 per row chunk too")
     ap.add_argument("--tp-one-stream", action="store_true",
                     help="copy-engine exchange: one push and one pull stream for all peers")
     ap.add_argument("--tp-mode", default="auto", choices=["auto", "ce", "fused", "nccl"],

@@ -130,16 +130,21 @@ int pkb200_stream_wait_value32(void* stream, const void* addr, unsigned int valu
 int pkb200_stream_write_value32(void* stream, void* addr, unsigned int value);
 
 /* Copy-engine tensor-parallel MLP exchange (new; the reference has no
- * multi-GPU path). W1 is column-split and W2 row-split over `world` ranks;
- * each rank calls pkb200_tp_ce_mlp_step after its GEMM1 (h = its [M, ffn/world]
- * shard of gelu(rmsnorm(x) @ W1 + b1)). The step runs GEMM2 in `chunks` row
- * chunks on `stream`; after each chunk the copy engines push every fp32
- * partial row block to the rank that owns it (slots), the owner sums the
- * slots in rank order with the b2 + residual epilogue, and the copy engines
- * gather the bf16 rows into `out` [M, d] on every rank.
+ * multi-GPU path). W1 is column-split and W2 row-split over `world` ranks.
+ * pkb200_tp_ce_mlp_block runs, in `chunks` row chunks on `stream`, GEMM1
+ * (xn = rmsnorm(x; gamma) [M, d] times this rank's W1 shard [d, ffn_shard],
+ * + b1, erf-GELU; into h_ws, bf16 [M/chunks, ffn_shard]) and GEMM2 (h times the
+ * W2 shard [ffn_shard, d] into fp32 partials); pkb200_tp_ce_mlp_step takes
+ * GEMM1's output h [M, ffn_shard] instead and runs GEMM2 alone in chunks.
+ * After each chunk's GEMM2 the copy engines push every fp32 partial row block
+ * to the rank that owns it (slots), the owner sums the slots in rank order
+ * with the b2 + residual epilogue into its gather buffer and pushes those
+ * bf16 rows into every peer's gather buffer (all NVLink traffic is writes);
+ * once all of a chunk has landed it is copied into `out` [M, d] on every rank.
+ * Each chunk's exchange overlaps the next chunk's GEMMs.
  * Buffers (peer pointers in this process's address space, e.g. from
  * pkb200_ipc_alloc / pkb200_ipc_open): slots[p] fp32 [chunks][world][M/chunks/world][d],
- * rows[p] bf16 [chunks][M/chunks/world][d], flags[p] uint32 [2][chunks][world]
+ * rows[p] bf16 [M][d] (gather buffer), flags[p] uint32 [2][chunks][world]
  * zeroed before first use, on every rank; y32 fp32 [M, d] and epoch_src
  * uint32 [2*8+2] local to this rank. `epoch` increases by 1 per step from 1.
  * pkb200_tp_ce_wait waits on the host for the last step, at most
@@ -163,10 +168,13 @@ int pkb200_tp_ce_destroy(void* plan);
 int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_shard,
                           const void* b2, const void* x, void* out, unsigned int epoch,
                           void* stream);
+int pkb200_tp_ce_mlp_block(void* plan, const void* xn, const void* w1, const void* b1,
+                           const void* w2, int ffn_shard, const void* b2, const void* x,
+                           void* out, void* h_ws, unsigned int epoch, void* stream);
 int pkb200_tp_ce_wait(void* plan, int timeout_ms);
-/* Number of exchange streams (push, pull and reduce) the last
- * pkb200_tp_ce_mlp_step joined back into the caller's stream: 2*(world-1)+1
- * with one push/pull stream per peer, 3 with one shared pair. */
+/* Number of exchange streams (push, pull, reduce and land) the last step
+ * joined back into the caller's stream: 2*(world-1)+2 with one push/pull
+ * stream per peer, 4 with one shared pair. */
 int pkb200_tp_ce_joined_streams(void* plan, int* count);
 
 /* out = rmsnorm(bf16(x + resid); weight, eps) over the last axis

@@ -45,6 +45,8 @@ SIGNATURES = {
                                     _P]),
     "pkb200_tp_ce_destroy": (c_int, [_P]),
     "pkb200_tp_ce_mlp_step": (c_int, [_P, _P, _P, c_int, _P, _P, _P, ctypes.c_uint, _P]),
+    "pkb200_tp_ce_mlp_block": (c_int, [_P, _P, _P, _P, _P, c_int, _P, _P, _P, _P, ctypes.c_uint,
+                                       _P]),
     "pkb200_tp_ce_wait": (c_int, [_P, c_int]),
     "pkb200_tp_ce_joined_streams": (c_int, [_P, ctypes.POINTER(c_int)]),
     "pkb200_quantize_fp8": (c_int, [_P, _P, c_longlong, c_int, _P]),

@@ -707,14 +707,17 @@ struct TpCePlan {
   int world = 0, rank = 0, chunks = 0, rows = 0, per = 0, d = 0, M = 0, device = 0;
   float* y32 = nullptr;                   // local GEMM2 partials [M, d]
   float* slots[kMaxPeers] = {};           // rank p's slots [chunks][world][per][d] fp32
-  bf16* mine[kMaxPeers] = {};             // rank p's reduced rows [chunks][per][d] bf16
+  bf16* gath[kMaxPeers] = {};             // rank p's gathered output [M][d] bf16
   unsigned* flags[kMaxPeers] = {};        // rank p's flags [2][chunks][world]
   unsigned* epoch_src = nullptr;          // local words [2 * kMaxPeers + 2]
   // one push and one pull stream per peer, or one of each for all peers
   int nstreams = 0;
-  cudaStream_t push[kMaxPeers] = {}, pull[kMaxPeers] = {}, red = nullptr, release = nullptr;
-  cudaEvent_t ev_gemm[kMaxTpChunks] = {}, ev_end[2 * kMaxPeers + 1] = {}, ev_step = nullptr,
-              ev_done = nullptr;
+  // push: fp32 partial blocks to their owners; pull (by name; it pushes): this
+  // rank's reduced rows into the peers' gather buffers
+  cudaStream_t push[kMaxPeers] = {}, pull[kMaxPeers] = {}, red = nullptr, land = nullptr,
+               release = nullptr;
+  cudaEvent_t ev_gemm[kMaxTpChunks] = {}, ev_red[kMaxTpChunks] = {}, ev_end[2 * kMaxPeers + 2] = {},
+              ev_step = nullptr, ev_done = nullptr;
   unsigned last_epoch = 0;
   int joined_streams = 0;                 // exchange streams joined into the caller's by the last step
   bool aborted = false;
@@ -728,8 +731,21 @@ struct TpCePlan {
   }
 };
 
-int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const bf16* bias,
-               const bf16* resid, bf16* out, unsigned epoch, cudaStream_t main) {
+// One tensor-parallel MLP step over the copy-engine exchange. GEMM1 (when w1
+// is given, per row chunk into h_ws; otherwise h holds it for all M rows) and
+// GEMM2 run in `chunks` row chunks on `main`. After GEMM2 of chunk i:
+//   push  every fp32 partial row block goes to its owner's slots, then a flag;
+//   red   the owner sums its slots in rank order with the b2 + residual
+//         epilogue into its own gather buffer;
+//   pull  the owner writes those bf16 rows into every peer's gather buffer,
+//         then a flag (all NVLink traffic is writes: copy engines reading
+//         peer memory while others write measured far slower);
+//   land  once every owner's rows of chunk i have landed, the chunk is copied
+//         from the gather buffer into `out`.
+// Chunk i's exchange overlaps GEMM1 and GEMM2 of chunk i+1.
+int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* xn, const bf16* w1, const bf16* b1,
+               bf16* h_ws, const bf16* w2, int ffn_shard, const bf16* bias, const bf16* resid,
+               bf16* out, unsigned epoch, cudaStream_t main) {
   const int W = pl->world, me = pl->rank, C = pl->chunks, rows = pl->rows, per = pl->per;
   const int d = pl->d;
   const size_t blk_f32 = static_cast<size_t>(per) * d * 4, blk_bf16 = static_cast<size_t>(per) * d * 2;
@@ -746,10 +762,10 @@ int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const
                ? 0 : static_cast<int>(cudaErrorUnknown);
   };
   int e;
-  // every stream starts after the caller's earlier work (h, x, out are ready)
+  // every stream starts after the caller's earlier work (h / xn, x, out are ready)
   if ((e = ck(cudaEventRecord(pl->ev_step, main)))) return e;
   // peers are visited from me+1 upwards (destinations staggered across ranks);
-  // `first` marks the first use of a stream when all peers share one
+  // with one shared stream pair only the first visit waits
   for (int k = 1; k < W; ++k) {
     const int p = (me + k) % W;
     if (pl->nstreams == 1 && k != 1) continue;
@@ -760,11 +776,18 @@ int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const
     if ((e = write_v(pl->push_for((me + k) % W), pl->epoch_src + (me + k) % W))) return e;
   if ((e = ck(cudaStreamWaitEvent(pl->red, pl->ev_step, 0)))) return e;
   if ((e = write_v(pl->red, pl->epoch_src + kMaxPeers))) return e;
+  if ((e = ck(cudaStreamWaitEvent(pl->land, pl->ev_step, 0)))) return e;
   for (int i = 0; i < C; ++i) {
     const size_t row0 = static_cast<size_t>(i) * rows;
     float* yc = pl->y32 + row0 * d;
-    if ((e = run_gemm<kEpiF32>(h + row0 * ffn_shard, w2, yc, rows, d, ffn_shard, EpilogueArgs{}, main)))
-      return e;
+    const bf16* hc = h ? h + row0 * ffn_shard : h_ws;
+    if (w1) {
+      EpilogueArgs ea{};
+      ea.bias = b1;
+      if ((e = run_gemm<kEpiBiasGelu>(xn + row0 * d, w1, h_ws, rows, ffn_shard, d, ea, main)))
+        return e;
+    }
+    if ((e = run_gemm<kEpiF32>(hc, w2, yc, rows, d, ffn_shard, EpilogueArgs{}, main))) return e;
     if ((e = ck(cudaEventRecord(pl->ev_gemm[i], main)))) return e;
     // push: my partial of p's row block -> p's slots[i][me], then the flag
     for (int k = 1; k < W; ++k) {
@@ -778,7 +801,8 @@ int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const
       if ((e = ck(cudaMemcpyAsync(pl->flag_rs(p, i, me), pl->epoch_src + p, 4, cudaMemcpyDefault, s))))
         return e;
     }
-    // reduce: own block in, wait for the peers' blocks, sum + epilogue, publish
+    // reduce: own block in, wait for the peers' blocks, sum + epilogue into
+    // my gather buffer
     cudaStream_t r = pl->red;
     if ((e = ck(cudaStreamWaitEvent(r, pl->ev_gemm[i], 0)))) return e;
     float* my_slots = pl->slots[me] + static_cast<size_t>(i) * W * per * d;
@@ -787,30 +811,35 @@ int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const
       return e;
     for (int k = 1; k < W; ++k)
       if ((e = wait_v(r, pl->flag_rs(me, i, (me + k) % W)))) return e;
-    bf16* rows_out = pl->mine[me] + static_cast<size_t>(i) * per * d;
     const size_t own0 = (row0 + static_cast<size_t>(me) * per) * d;
-    if ((e = pkb200_reduce_slots_bias_residual(my_slots, W, per, d, bias, resid + own0, rows_out, r)))
+    if ((e = pkb200_reduce_slots_bias_residual(my_slots, W, per, d, bias, resid + own0,
+                                               pl->gath[me] + own0, r)))
       return e;
-    if ((e = ck(cudaMemcpyAsync(out + own0, rows_out, blk_bf16, cudaMemcpyDefault, r)))) return e;
+    if ((e = ck(cudaEventRecord(pl->ev_red[i], r)))) return e;
+    // pull streams: my reduced rows of chunk i -> every peer's gather buffer, then the flag
     for (int k = 1; k < W; ++k) {
-      const int p = (me + k) % W;
-      if ((e = ck(cudaMemcpyAsync(pl->flag_ag(p, i, me), pl->epoch_src + kMaxPeers, 4, cudaMemcpyDefault, r))))
-        return e;
-    }
-    // pull: p's reduced rows of chunk i -> my output
-    for (int k = 1; k < W; ++k) {
-      const int p = (me + W - k) % W;  // pull first from the peer that pushed to me first
+      const int p = (me + W - k) % W;  // write first to the peer that pushed to me first
       cudaStream_t s = pl->pull_for(p);
-      if ((e = wait_v(s, pl->flag_ag(me, i, p)))) return e;
-      const size_t dst0 = (row0 + static_cast<size_t>(p) * per) * d;
-      if ((e = ck(cudaMemcpyAsync(out + dst0, pl->mine[p] + static_cast<size_t>(i) * per * d, blk_bf16,
+      if ((pl->nstreams > 1 || k == 1) && (e = ck(cudaStreamWaitEvent(s, pl->ev_red[i], 0))))
+        return e;
+      if ((e = ck(cudaMemcpyAsync(pl->gath[p] + own0, pl->gath[me] + own0, blk_bf16,
+                                  cudaMemcpyDefault, s))))
+        return e;
+      if ((e = ck(cudaMemcpyAsync(pl->flag_ag(p, i, me), pl->epoch_src + kMaxPeers, 4,
                                   cudaMemcpyDefault, s))))
         return e;
     }
+    // land: chunk i complete in my gather buffer -> out
+    cudaStream_t l = pl->land;
+    if ((e = ck(cudaStreamWaitEvent(l, pl->ev_red[i], 0)))) return e;
+    for (int k = 1; k < W; ++k)
+      if ((e = wait_v(l, pl->flag_ag(me, i, (me + k) % W)))) return e;
+    if ((e = ck(cudaMemcpyAsync(out + row0 * d, pl->gath[me] + row0 * d,
+                                static_cast<size_t>(rows) * d * 2, cudaMemcpyDefault, l))))
+      return e;
   }
-  // the caller's stream continues once every copy and the last reduce are done
   // One join event per push/pull stream used (k counts them) plus the reduce
-  // stream's; every peer's streams are joined when each peer has its own.
+  // and land streams'; every peer's streams are joined when each peer has its own.
   int k = 0;
   for (int jp = 1; jp < W; ++jp) {
     const int p = (me + jp) % W;
@@ -821,11 +850,14 @@ int tp_ce_step(TpCePlan* pl, const bf16* h, const bf16* w2, int ffn_shard, const
       ++k;
     }
   }
-  if ((e = ck(cudaEventRecord(pl->ev_end[k], pl->red)))) return e;
-  if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k], 0)))) return e;
-  pl->joined_streams = k + 1;
-  // every push and pull stream (one pair per peer, or one pair) plus the reduce stream
-  if (pl->joined_streams != 2 * (pl->nstreams == 1 ? 1 : W - 1) + 1) return cudaErrorUnknown;
+  for (cudaStream_t s : {pl->red, pl->land}) {
+    if ((e = ck(cudaEventRecord(pl->ev_end[k], s)))) return e;
+    if ((e = ck(cudaStreamWaitEvent(main, pl->ev_end[k], 0)))) return e;
+    ++k;
+  }
+  pl->joined_streams = k;
+  // every push and pull stream (one pair per peer, or one pair) plus reduce and land
+  if (pl->joined_streams != 2 * (pl->nstreams == 1 ? 1 : W - 1) + 2) return cudaErrorUnknown;
   pl->last_epoch = epoch;
   return ck(cudaEventRecord(pl->ev_done, main));
 }
@@ -998,7 +1030,7 @@ int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_p
     if (!slots[p] || !rows[p] || !flags[p] || !aligned16(slots[p]) || !aligned16(rows[p]))
       return cudaErrorInvalidValue;
     pl->slots[p] = slots[p];
-    pl->mine[p] = static_cast<bf16*>(rows[p]);
+    pl->gath[p] = static_cast<bf16*>(rows[p]);
     pl->flags[p] = flags[p];
   }
   int e = cudaGetDevice(&pl->device);
@@ -1014,10 +1046,13 @@ int pkb200_tp_ce_create(int world, int rank, int M, int d, int chunks, int per_p
     }
     // the reduce kernels go ahead of the next GEMM chunk's CTAs when SMs free up
     if ((r = cudaStreamCreateWithPriority(&pl->red, cudaStreamNonBlocking, hi))) return r;
+    if ((r = cudaStreamCreateWithFlags(&pl->land, cudaStreamNonBlocking))) return r;
     if ((r = cudaStreamCreateWithFlags(&pl->release, cudaStreamNonBlocking))) return r;
-    for (int i = 0; i < chunks; ++i)
+    for (int i = 0; i < chunks; ++i) {
       if ((r = cudaEventCreateWithFlags(&pl->ev_gemm[i], cudaEventDisableTiming))) return r;
-    for (int i = 0; i < 2 * kMaxPeers + 1; ++i)
+      if ((r = cudaEventCreateWithFlags(&pl->ev_red[i], cudaEventDisableTiming))) return r;
+    }
+    for (int i = 0; i < 2 * kMaxPeers + 2; ++i)
       if ((r = cudaEventCreateWithFlags(&pl->ev_end[i], cudaEventDisableTiming))) return r;
     if ((r = cudaEventCreateWithFlags(&pl->ev_step, cudaEventDisableTiming))) return r;
     return cudaEventCreateWithFlags(&pl->ev_done, cudaEventDisableTiming);
@@ -1038,8 +1073,10 @@ int pkb200_tp_ce_destroy(void* plan) {
     if (pl->pull[i]) cudaStreamDestroy(pl->pull[i]);
   }
   if (pl->red) cudaStreamDestroy(pl->red);
+  if (pl->land) cudaStreamDestroy(pl->land);
   if (pl->release) cudaStreamDestroy(pl->release);
   for (auto ev : pl->ev_gemm) if (ev) cudaEventDestroy(ev);
+  for (auto ev : pl->ev_red) if (ev) cudaEventDestroy(ev);
   for (auto ev : pl->ev_end) if (ev) cudaEventDestroy(ev);
   if (pl->ev_step) cudaEventDestroy(pl->ev_step);
   if (pl->ev_done) cudaEventDestroy(pl->ev_done);
@@ -1054,9 +1091,24 @@ int pkb200_tp_ce_mlp_step(void* plan, const void* h, const void* w2, int ffn_sha
   if (!pl || !h || !w2 || !b2 || !x || !out || ffn_shard <= 0) return cudaErrorInvalidValue;
   if (pl->aborted) return cudaErrorLaunchFailure;
   if (epoch == 0 || static_cast<int>(epoch - pl->last_epoch) <= 0) return cudaErrorInvalidValue;
-  const int e = tp_ce_step(pl, cb(h), cb(w2), ffn_shard, cb(b2), cb(x), b(out), epoch, S(stream));
+  const int e = tp_ce_step(pl, cb(h), nullptr, nullptr, nullptr, nullptr, cb(w2), ffn_shard,
+                          cb(b2), cb(x), b(out), epoch, S(stream));
   // a step that failed half-way may have left flag waits queued on the side
   // streams that no peer will satisfy: the plan is not reused
+  if (e) pl->aborted = true;
+  return e;
+}
+
+int pkb200_tp_ce_mlp_block(void* plan, const void* xn, const void* w1, const void* b1,
+                           const void* w2, int ffn_shard, const void* b2, const void* x,
+                           void* out, void* h_ws, unsigned int epoch, void* stream) {
+  auto* pl = static_cast<TpCePlan*>(plan);
+  if (!pl || !xn || !w1 || !b1 || !w2 || !b2 || !x || !out || !h_ws || ffn_shard <= 0)
+    return cudaErrorInvalidValue;
+  if (pl->aborted) return cudaErrorLaunchFailure;
+  if (epoch == 0 || static_cast<int>(epoch - pl->last_epoch) <= 0) return cudaErrorInvalidValue;
+  const int e = tp_ce_step(pl, nullptr, cb(xn), cb(w1), cb(b1), b(h_ws), cb(w2), ffn_shard,
+                          cb(b2), cb(x), b(out), epoch, S(stream));
   if (e) pl->aborted = true;
   return e;
 }

@@ -13,10 +13,11 @@ the rows of GEMM2 are processed in chunks whose reduction (reduce-scatter of
 the fp32 partials, epilogue on this rank's rows, all-gather of the bf16
 result) overlaps GEMM2 of the next chunk. Three exchanges implement it:
 
-* "copy_engine" (pkb200_tp_ce_*): the copy engines push each partial row block
-  into its owner's slot buffer (plain device memory mapped into every peer with
-  CUDA IPC handles) with an epoch flag behind it; the owner waits on the flags with stream memory operations, sums
-  the slots and publishes its rows, which the peers' copy engines pull. No SM
+* "copy_engine" (pkb200_tp_ce_*): GEMM1 and GEMM2 run in row chunks; the copy
+  engines push each fp32 partial row block into its owner's slot buffer (plain
+  device memory mapped into every peer with CUDA IPC handles) with an epoch
+  flag behind it; the owner waits on the flags with stream memory operations,
+  sums the slots and writes its rows into every peer's gather buffer. No SM
   is spent on data movement, so the persistent GEMM keeps every SM.
 * "nccl": NCCL reduce-scatter + all-gather on a side stream.
 * "peer_store": the GEMM2 epilogue itself stores the partial tiles into the
@@ -55,7 +56,7 @@ class TensorParallelMLP:
 
     def __init__(self, gamma, w1_shard, b1_shard, w2_shard, b2, eps=1e-6, group=None, kern=None,
                  chunks=1, fused_reduce=False, comm_sms=0, reduce=None, per_peer_streams=True,
-                 timeout_ms=60000):
+                 timeout_ms=60000, gemm1_chunked=False):
         if kern is None:
             from . import ops as kern
         self.kern = kern
@@ -70,6 +71,9 @@ class TensorParallelMLP:
             raise ValueError(f"reduce must be one of {self.REDUCERS}, got {self.reduce!r}")
         self.fused_reduce = self.reduce == "peer_store"
         self.per_peer_streams = per_peer_streams
+        # copy-engine exchange: run GEMM1 per row chunk too (the exchanges then
+        # overlap GEMM1 as well; row chunks of GEMM1 quantise worse on the SMs)
+        self.gemm1_chunked = gemm1_chunked
         self.timeout_ms = timeout_ms
         self._ce = None
         self._epoch = 0
@@ -97,15 +101,17 @@ class TensorParallelMLP:
     def _forward(self, x, out=None):
         k = self.kern
         xn = k.rmsnorm(x, self.gamma, self.eps)
+        if self.world > 1 and self.reduce == "copy_engine" and x.is_cuda and self.gemm1_chunked:
+            return self._copy_engine(x, xn, x.shape[0], out, gemm1=True)
         h = k.fused_matmul_bias_gelu(xn, self.w1, self.b1)
         if self.world == 1:
             y32 = k.matmul_f32out(h, self.w2)
             return k.bias_residual_f32(y32, self.b2, x)
         M = h.shape[0]
+        if self.reduce == "copy_engine" and x.is_cuda:
+            return self._copy_engine(x, h, M, out, gemm1=False)
         if self.reduce == "peer_store" and x.is_cuda:
             return self._fused(x, h, M)
-        if self.reduce == "copy_engine" and x.is_cuda:
-            return self._copy_engine(x, h, M, out)
         if self.chunks == 1 or not x.is_cuda:
             y32 = k.matmul_f32out(h, self.w2)
             dist.all_reduce(y32, group=self.group)
@@ -215,7 +221,7 @@ class TensorParallelMLP:
         if rows * C != M or rows % W:
             raise ValueError(f"M={M} must split into {C} chunks of a multiple of {W} rows")
         per = rows // W
-        sizes = (C * W * per * d * 4, C * per * d * 2, (2 * C * W + 4) * 4)  # slots, rows, flags
+        sizes = (C * W * per * d * 4, M * d * 2, (2 * C * W + 4) * 4)  # slots, gather, flags
         own, handles = [], []
         for nbytes in sizes:
             p = ctypes.c_void_p()
@@ -251,17 +257,31 @@ class TensorParallelMLP:
         self._epoch = 0
         return self._ce
 
-    def _copy_engine(self, x, h, M, out=None):
+    def _copy_engine(self, x, a, M, out=None, gemm1=False):
+        """a: GEMM1's output h [M, ffn_shard], or (gemm1=True) rmsnorm(x) whose
+        GEMM1 then runs per row chunk inside the exchange step."""
         from ._lib import check, lib
         d = self.w2.shape[1]
+        F = self.w1.shape[1]
         ce = self._ce_plan(x, M, d)
         self._epoch += 1
         if out is None:
             out = torch.empty_like(x)
-        check(lib().pkb200_tp_ce_mlp_step(ce["plan"], h.data_ptr(), self.w2.data_ptr(), h.shape[1],
-                                          self.b2.data_ptr(), x.data_ptr(), out.data_ptr(),
-                                          self._epoch, torch.cuda.current_stream().cuda_stream),
-              "tp_ce_mlp_step")
+        stream = torch.cuda.current_stream().cuda_stream
+        if not gemm1:
+            check(lib().pkb200_tp_ce_mlp_step(ce["plan"], a.data_ptr(), self.w2.data_ptr(), F,
+                                              self.b2.data_ptr(), x.data_ptr(), out.data_ptr(),
+                                              self._epoch, stream), "tp_ce_mlp_step")
+            return out
+        xn = a
+        rows = M // self.chunks
+        if ce.get("h_ws") is None or ce["h_ws"].shape != (rows, F):
+            ce["h_ws"] = torch.empty(rows, F, dtype=x.dtype, device=x.device)
+        check(lib().pkb200_tp_ce_mlp_block(ce["plan"], xn.data_ptr(), self.w1.data_ptr(),
+                                           self.b1.data_ptr(), self.w2.data_ptr(), F,
+                                           self.b2.data_ptr(), x.data_ptr(), out.data_ptr(),
+                                           ce["h_ws"].data_ptr(), self._epoch, stream),
+              "tp_ce_mlp_block")
         return out
 
     def joined_streams(self):

@@ -36,16 +36,17 @@ def _run(mode, port, nproc=2):
 def test_tp_exchanges_match_single_gpu(nproc):
     res = _run("parity", 29711 + nproc, nproc)
     print(res)
-    for name in ("copy_engine", "copy_engine_one_stream", "nccl", "peer_store"):
+    for name in ("copy_engine", "copy_engine_gemm1_chunked", "copy_engine_one_stream", "nccl",
+                 "peer_store"):
         # the only change from one GPU is the fp32 summation order of the partials
         assert res[name]["bit_exact"] >= 0.93, (name, res[name])
         assert res[name]["max_err_over_scale"] <= 2.0 ** -6, (name, res[name])
         # each rank's row block arrives (own reduce and every peer's pulled rows)
         assert min(res[name + "_blocks_exact"]) >= 0.9, (name, res[name + "_blocks_exact"])
-    assert res["copy_engine_joined_streams"] == 2 * (nproc - 1) + 1
-    assert res["copy_engine_one_stream_joined_streams"] == 3
+    assert res["copy_engine_joined_streams"] == 2 * (nproc - 1) + 2
+    assert res["copy_engine_one_stream_joined_streams"] == 4
     assert res["ranks_agree"]
-    assert res["ce_eq_one_stream"] and res["ce_eq_peer_store"]
+    assert res["ce_eq_one_stream"] and res["ce_eq_peer_store"] and res["ce_eq_gemm1_chunked"]
     assert res["device_error"] == 0
 
 

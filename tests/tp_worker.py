@@ -49,6 +49,7 @@ def parity(rank, world, host):
     w1s, b1s, w2s = shard_weights(W1, b1, W2, rank, world)
     outs, res = {}, {}
     for name, kw in (("copy_engine", dict(reduce="copy_engine")),
+                     ("copy_engine_gemm1_chunked", dict(reduce="copy_engine", gemm1_chunked=True)),
                      ("copy_engine_one_stream", dict(reduce="copy_engine", per_peer_streams=False)),
                      ("nccl", dict(reduce="nccl")),
                      ("peer_store", dict(reduce="peer_store"))):
@@ -77,6 +78,7 @@ def parity(rank, world, host):
     res["ranks_agree"] = all(torch.equal(g, gathered[0]) for g in gathered)
     # both copy-engine variants and the peer-store path sum the slots in rank order
     res["ce_eq_one_stream"] = torch.equal(outs["copy_engine"], outs["copy_engine_one_stream"])
+    res["ce_eq_gemm1_chunked"] = torch.equal(outs["copy_engine"], outs["copy_engine_gemm1_chunked"])
     res["ce_eq_peer_store"] = torch.equal(outs["copy_engine"], outs["peer_store"])
     res["device_error"] = pk.device_error()
     return res
