@@ -721,6 +721,10 @@ PROFILE_CASES = {
     "gemm1c5": "fused_matmul_bias_gelu at config-5 GEMM1 shape with M=4096 (d=8192, ffn=28672)",
     "gemm2c5": "matmul + bias + residual (mlp GEMM2 epilogue) at config-5 GEMM2 shape, M=4096",
     "gemm": "plain matmul 2048 x 4096 x 16384 (config-2 GEMM1 shape)",
+    "rmsnorm_c5": "rmsnorm with gamma over config-5 X (16384 x 8192)",
+    "int8c4": "matmul_int8 at config-4 GEMM1 shape (4096 x 4096 x 14336): expansion + GEMM",
+    "fp8c4": "matmul_fp8 (e4m3 weights) at config-4 GEMM1 shape: expansion + GEMM",
+    "tp_reduce8": "copy-engine exchange's owner reduce: 8 fp32 slots of 512 x 8192 + b2 + residual",
 }
 
 
@@ -748,6 +752,33 @@ def run_profile_case(which):
         x = torch.randn(4096, 8192, device=dev).bfloat16()
         for _ in range(3):
             pk.ops.matmul_bias_residual(h, w2, b2, x)
+    elif which == "rmsnorm_c5":
+        x = torch.randn(16384, 8192, device=dev).bfloat16()
+        g = (1 + 0.1 * torch.randn(8192, device=dev)).bfloat16()
+        for _ in range(3):
+            pk.ops.rmsnorm(x, g, 1e-6)
+    elif which in ("int8c4", "fp8c4"):
+        a = torch.randn(4096, 4096, device=dev).bfloat16()
+        if which == "int8c4":
+            wq = torch.randint(-127, 128, (4096, 14336), device=dev, dtype=torch.int8)
+            sc = (0.001 + 0.019 * torch.rand(14336, device=dev)).bfloat16().float()
+            for _ in range(3):
+                pk.ops.matmul_int8(a, wq, sc)
+        else:
+            w8 = pk.ops.quantize_fp8((torch.randn(4096, 14336, device=dev) / 64).bfloat16(), "e4m3")
+            for _ in range(3):
+                pk.ops.matmul_fp8(a, w8)
+    elif which == "tp_reduce8":
+        from polykernel_b200._lib import check, lib
+        W, per, d = 8, 512, 8192
+        slots = torch.randn(W, per, d, device=dev)
+        b2 = (0.02 * torch.randn(d, device=dev)).bfloat16()
+        x = torch.randn(per, d, device=dev).bfloat16()
+        out = torch.empty_like(x)
+        for _ in range(3):
+            check(lib().pkb200_reduce_slots_bias_residual(
+                slots.data_ptr(), W, per, d, b2.data_ptr(), x.data_ptr(), out.data_ptr(),
+                torch.cuda.current_stream().cuda_stream), "reduce_slots_bias_residual")
     elif which == "gemm":
         a = torch.randn(2048, 4096, device=dev).bfloat16()
         b = (torch.randn(4096, 16384, device=dev) / 64).bfloat16()
