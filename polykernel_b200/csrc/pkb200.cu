@@ -415,10 +415,20 @@ int run_rmsnorm(const bf16* x, const bf16* w, bf16* y, long long rows, int cols,
   if (rows < 0 || cols < 0) return cudaErrorInvalidValue;
   if (rows == 0 || cols == 0) return cudaSuccess;
   if (!x || !y) return cudaErrorInvalidValue;
-  const int rows_per_block = 8;
-  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
-  rmsnorm_rows_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, s>>>(x, w, y, rows,
-                                                                                   cols, eps);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (cols % 8 == 0 && cols > 1024 && cols <= 8192 && al(x) && al(y) && (!w || al(w)) &&
+      rows <= 0x7fffffffLL) {
+    // the row stays in registers: one HBM read per element
+    const unsigned g = static_cast<unsigned>(rows);
+    if (cols <= 2048) rmsnorm_rows_reg_kernel<1><<<g, 256, 0, s>>>(x, w, y, cols, eps);
+    else if (cols <= 4096) rmsnorm_rows_reg_kernel<2><<<g, 256, 0, s>>>(x, w, y, cols, eps);
+    else rmsnorm_rows_reg_kernel<4><<<g, 256, 0, s>>>(x, w, y, cols, eps);
+  } else {
+    const int rows_per_block = 8;
+    const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+    rmsnorm_rows_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, s>>>(x, w, y, rows,
+                                                                                     cols, eps);
+  }
   g_counters[kCntOther]++;
   return cudaGetLastError();
 }

@@ -112,6 +112,71 @@ __global__ void rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// Same operation with the row held in registers: one 256-thread CTA per row,
+// thread t owns 16-byte chunks t, t+256, ... (CH of them), so the row is read
+// from HBM once (the warp-per-row kernel above reads it twice, and at 16 KB
+// rows the second read misses L2). Requires cols % 8 == 0, cols <= 2048*CH and
+// 16-byte aligned pointers.
+template <int CH>
+__global__ void __launch_bounds__(256) rmsnorm_rows_reg_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ weight,
+    __nv_bfloat16* __restrict__ out, int cols, float eps) {
+  __shared__ float red[8];
+  const long long r = blockIdx.x;
+  const int t = threadIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * cols);
+  uint4* yr = reinterpret_cast<uint4*>(out + r * cols);
+  const int nch = cols >> 3;
+  uint4 v[CH];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const int c = t + 256 * j;
+    v[j] = c < nch ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(w4[q]);
+      ss += f.x * f.x;
+      ss += f.y * f.y;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  if (t < 32) {
+    float a = t < 8 ? red[t] : 0.f;
+    a = warp_sum(a);
+    if (t == 0) red[0] = a;
+  }
+  __syncthreads();
+  const float rms = sqrtf(red[0] / static_cast<float>(cols) + eps);
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const int c = t + 256 * j;
+    if (c >= nch) break;
+    const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    uint32_t g4[4] = {0, 0, 0, 0};
+    if (weight) {
+      const uint4 g = reinterpret_cast<const uint4*>(weight)[c];
+      g4[0] = g.x; g4[1] = g.y; g4[2] = g.z; g4[3] = g.w;
+    }
+    uint32_t o4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(w4[q]);
+      float a = __fdiv_rn(f.x, rms), b = __fdiv_rn(f.y, rms);
+      if (weight) {
+        const float2 g = unpack_bf16x2(g4[q]);
+        a *= g.x;
+        b *= g.y;
+      }
+      o4[q] = pack_bf16x2(a, b);
+    }
+    yr[c] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+}
+
 // ------------------------------------------------- residual add + RMSNorm --
 // t = bf16(x + resid) (golden.add), out = rmsnorm(t; weight, eps)
 // (golden.fused_residual_rmsnorm, golden.py:108-112). `sum_out` (nullable)

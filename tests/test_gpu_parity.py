@@ -345,3 +345,22 @@ def test_attention_append_with_fallback_keeps_cache_bf16(pk):
     check_attention(f32_from_t(o), ref, s_kv=Sc + Sn,
                     ref64_f32=O.attention_prefill(F(q), keys, vals, True, acc=np.float64))
     assert pk.device_error() == 0
+
+
+@pytest.mark.parametrize("cols", [1032, 4096, 8192])
+@pytest.mark.parametrize("with_gamma", [True, False])
+def test_rmsnorm_wide_rows_vs_oracle(pk, cols, with_gamma):
+    """Rows of 1025..8192 columns take the register-resident kernel (one CTA per
+    row); same rounding as the golden (golden.py:83-90)."""
+    rng = np.random.default_rng(cols)
+    x = _rand_bits(rng, (67, cols))
+    g = _rand_bits(rng, (cols,), 0.1, 1.0) if with_gamma else None
+    c0 = _counters(pk)
+    out = pk.ops.rmsnorm(t_from_bits(x), t_from_bits(g) if with_gamma else None, 1e-6)
+    assert _used(pk, c0, "other")
+    ref = O.rmsnorm(F(x), F(g) if with_gamma else None, 1e-6)
+    got = f32_from_t(out)
+    assert np.mean(got == ref) >= 0.99
+    # any difference is one bf16 ulp (the fp32 sum of squares in another order)
+    diff = np.abs(got - ref)
+    assert np.all(diff <= 2.0 ** -7 * np.abs(ref) + 1e-30)
