@@ -318,6 +318,20 @@ int polykernel_fused_mlp_block(float* in, float* out, int M, int N, int K);
  * tensor-core kernels set on timeout (0 = none). Synchronises the device. */
 int pkb200_device_error(int* code);
 
+/* The MLP block followed by the next layer's RMSNorm (new; the survey's "next"
+ * row f1, golden.fused_residual_rmsnorm, golden.py:108-112): Y = the MLP block
+ * output (the residual stream, as pkb200_mlp_block) and
+ * Yn = bf16(Y / sqrt(mean(Y^2) + eps_next) * gamma_next) (gamma_next may be
+ * NULL). GEMM2's epilogue also writes each row's partial sums of squares of the
+ * rounded Y, so the normalisation is one elementwise pass over Y with no row
+ * reduction. Workspace: pkb200_mlp_block_rmsnorm_next_workspace_size bytes. */
+size_t pkb200_mlp_block_rmsnorm_next_workspace_size(int M, int d, int ffn);
+int pkb200_mlp_block_rmsnorm_next(const void* X, const void* gamma, const void* W1,
+                                  const void* b1, const void* W2, const void* b2,
+                                  const void* gamma_next, void* Y, void* Yn, int M, int d, int ffn,
+                                  float eps, float eps_next, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* Number of tensor-core attention CTAs, since load on the current device, that
  * recomputed their query rows with the exact fp32 row routine because a V
  * tile held values the fp16 P.V pass cannot carry exactly (|v| >= 2^16,

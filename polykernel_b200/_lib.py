@@ -76,6 +76,9 @@ SIGNATURES = {
     "pkb200_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "pkb200_path_counters": (c_int, [ctypes.POINTER(c_longlong), c_int]),
     "pkb200_attention_exact_ctas": (c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
+    "pkb200_mlp_block_rmsnorm_next_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "pkb200_mlp_block_rmsnorm_next": (c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int,
+                                              c_int, c_float, c_float, _P, c_size_t, _P]),
 }
 
 _lib = None

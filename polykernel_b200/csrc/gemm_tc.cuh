@@ -37,6 +37,14 @@ enum EpilogueKind : int {
   kEpiPeerStoreF32 = 6,  // owner(m).slot[src_rank][m % rows_per_rank, n] = acc (plain stores;
                          // the owner sums the slots afterwards)
   kEpiQkvScatter = 7,    // bf16(acc) written to Q/K/V in [B, H, S, Dh] layout
+  // int8 weight-only chain (quant_golden.matmul_int8, then the golden bias /
+  // gelu / add, each rounded): the matmul's per-column scale, then as kinds 1/2
+  kEpiScaleBiasGelu = 8,   // C = bf16(gelu(bf16(bf16(acc * s[n]) + bias)))
+  kEpiScaleBiasResid = 9,  // C = bf16(bf16(bf16(acc * s[n]) + bias) + resid)
+  // MLP GEMM2 feeding the next layer's RMSNorm (golden.fused_residual_rmsnorm,
+  // golden.py:108-112): C as kEpiBiasResid, plus each (row, N tile, column
+  // half)'s fp32 sum of squares of the rounded outputs into row_ss
+  kEpiBiasResidSS = 10,
 };
 
 constexpr int kMaxPeers = 8;
@@ -62,6 +70,9 @@ struct EpilogueArgs {
   // kEpiQkvScatter: row m = b*seq + s, column n = which*heads*head_dim + h*head_dim + e
   __nv_bfloat16* qkv[3];
   int seq, heads, head_dim;
+  // kEpiBiasResidSS: row_ss[m * ss_stride + 2 * n_tile + half]
+  float* row_ss;
+  int ss_stride;
 };
 
 
@@ -104,7 +115,7 @@ __device__ __forceinline__ uint4 epilogue8(const float (&acc)[8], const Epilogue
       v[2 * j] = gelu_erf(u0);
       v[2 * j + 1] = gelu_erf(u1);
     }
-  } else if constexpr (EPI == kEpiBiasResid) {
+  } else if constexpr (EPI == kEpiBiasResid || EPI == kEpiBiasResidSS) {
     const uint4 b = __ldg(reinterpret_cast<const uint4*>(ea.bias + n));
     const uint4 r = *reinterpret_cast<const uint4*>(ea.resid + m * ea.ld_resid + n);
     const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
@@ -121,6 +132,31 @@ __device__ __forceinline__ uint4 epilogue8(const float (&acc)[8], const Epilogue
     const float4 s1 = __ldg(reinterpret_cast<const float4*>(ea.col_scale + n + 4));
     v[0] = acc[0] * s0.x; v[1] = acc[1] * s0.y; v[2] = acc[2] * s0.z; v[3] = acc[3] * s0.w;
     v[4] = acc[4] * s1.x; v[5] = acc[5] * s1.y; v[6] = acc[6] * s1.z; v[7] = acc[7] * s1.w;
+  } else if constexpr (EPI == kEpiScaleBiasGelu || EPI == kEpiScaleBiasResid) {
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(ea.col_scale + n));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(ea.col_scale + n + 4));
+    const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(ea.bias + n));
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t rw[4] = {0u, 0u, 0u, 0u};
+    if constexpr (EPI == kEpiScaleBiasResid) {
+      const uint4 r = *reinterpret_cast<const uint4*>(ea.resid + m * ea.ld_resid + n);
+      rw[0] = r.x; rw[1] = r.y; rw[2] = r.z; rw[3] = r.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 bb = unpack_bf16x2(bw[j]);
+      const float u0 = bf16_round(bf16_round(acc[2 * j] * sc[2 * j]) + bb.x);
+      const float u1 = bf16_round(bf16_round(acc[2 * j + 1] * sc[2 * j + 1]) + bb.y);
+      if constexpr (EPI == kEpiScaleBiasGelu) {
+        v[2 * j] = gelu_erf(u0);
+        v[2 * j + 1] = gelu_erf(u1);
+      } else {
+        const float2 rr = unpack_bf16x2(rw[j]);
+        v[2 * j] = u0 + rr.x;
+        v[2 * j + 1] = u1 + rr.y;
+      }
+    }
   } else {
     // kinds whose tiles never reach this packer (fp32 and peer-store outputs)
 #pragma unroll
@@ -355,6 +391,7 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       tc_fence_after();
       const long long m = static_cast<long long>(mb) * BM + row;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      float ss_row = 0.f;  // kEpiBiasResidSS: this thread's share of the row's sum of squares
 #pragma unroll 1
       for (int cc = 0; cc < BN / 64; ++cc) {
         const int c = half * (BN / 64) + cc;
@@ -408,10 +445,22 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
               } else {
                 const uint4 o = epilogue8<EPI>(a8, ea, m, n);
                 *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(C) + m * ldc + n) = o;
+                if constexpr (EPI == kEpiBiasResidSS) {
+                  const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    const float2 f = unpack_bf16x2(ow[k]);
+                    ss_row = fmaf(f.x, f.x, ss_row);
+                    ss_row = fmaf(f.y, f.y, ss_row);
+                  }
+                }
               }
             }
           }
         }
+      }
+      if constexpr (EPI == kEpiBiasResidSS) {
+        if (m < M) ea.row_ss[m * ea.ss_stride + 2 * nb + half] = ss_row;
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);

@@ -19,6 +19,7 @@
 #include <utility>
 
 #include "attention_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "fp8.cuh"
 #include "simt_kernels.cuh"
 #include "tuning.h"
@@ -176,17 +177,23 @@ const char* op_name(int epi) {
     case kEpiColScale: return "matmul_int8";
     case kEpiF32: return "matmul_f32out";
     case kEpiQkvScatter: return "qkv_projection";
+    case kEpiScaleBiasGelu: return "matmul_int8_bias_gelu";
+    case kEpiScaleBiasResid: return "matmul_int8_bias_residual";
+    case kEpiBiasResidSS: return "matmul_bias_residual";
     default: return "matmul_peer_store_f32";
   }
 }
 
 // The compiled tensor-core GEMM variants, as tuning-cache configs
-// (block_m 128, block_k 64, 10 warps, 16-byte vectors = 8 bf16, 2 TMEM
-// accumulators; block_n and shared_memory_stages vary).
+// (block_k 64, 10 warps, 16-byte vectors = 8 bf16, 2 TMEM accumulators;
+// block_n and shared_memory_stages vary; block_m 256 = the CTA-pair kernel).
 int variant_of(const tuning::Config& c) {
-  if (c.block_m != gemm::BM || c.block_k != gemm::BK || c.num_warps != gemm::NUM_THREADS / 32 ||
-      c.vector_width != 8 || c.unroll != 2)
+  if (c.block_k != gemm::BK || c.num_warps != gemm::NUM_THREADS / 32 || c.vector_width != 8 ||
+      c.unroll != 2)
     return -1;
+  if (c.block_m == 2 * gemm::BM)
+    return c.block_n == 256 && c.shared_memory_stages == 6 ? 4 : -1;
+  if (c.block_m != gemm::BM) return -1;
   if (c.block_n == 256 && c.shared_memory_stages == 4) return 0;
   if (c.block_n == 256 && c.shared_memory_stages == 3) return 1;
   if (c.block_n == 128 && c.shared_memory_stages == 4) return 2;
@@ -294,6 +301,25 @@ int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, i
   return cudaGetLastError();
 }
 
+template <int EPI, int STAGES>
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N, int K,
+                     const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di) {
+  constexpr int smem = gemm2::smem_bytes(STAGES);
+  if (const int e = ensure_smem_attr(reinterpret_cast<const void*>(gemm_tc2_kernel<EPI, STAGES>),
+                                     smem))
+    return e;
+  const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+  long long grid = di->sms & ~1;  // whole CTA pairs
+  const int cap = g_gemm_max_ctas.load();
+  if (cap > 0 && cap < grid) grid = cap & ~1;
+  if (2 * tiles < grid) grid = 2 * tiles;
+  if (grid < 2) grid = 2;
+  gemm_tc2_kernel<EPI, STAGES><<<static_cast<unsigned>(grid), gemm2::NUM_THREADS, smem, s>>>(
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
+  g_counters[kCntGemmTc]++;
+  return cudaGetLastError();
+}
+
 template <int EPI>
 int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
                    const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di) {
@@ -332,6 +358,9 @@ int launch_gemm_tc(const bf16* A, const bf16* B, void* C, int M, int N, int K,
       g_last_cfg = cfg;
     }
     switch (variant_of(cfg)) {
+      case 4:
+        if constexpr (EPI != kEpiQkvScatter) return launch_gemm_pair<EPI, 6>(ma, mb, C, M, N, K, ea, s, di);
+        return launch_gemm_variant<EPI, 256, 4>(ma, mb, C, M, N, K, ea, s, di);
       case 1: return launch_gemm_variant<EPI, 256, 3>(ma, mb, C, M, N, K, ea, s, di);
       case 2: return launch_gemm_variant<EPI, 128, 4>(ma, mb, C, M, N, K, ea, s, di);
       case 3: return launch_gemm_variant<EPI, 128, 6>(ma, mb, C, M, N, K, ea, s, di);
@@ -355,11 +384,16 @@ int run_gemm(const bf16* A, const bf16* B, void* C, int M, int N, int K, const E
   if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
   if (M == 0 || N == 0) return cudaSuccess;
   if (!A || !B || !C) return cudaErrorInvalidValue;
-  if (EPI == kEpiBiasGelu || EPI == kEpiBiasResid) {
-    if (!ea.bias) return cudaErrorInvalidValue;
-  }
-  if (EPI == kEpiBiasResid && !ea.resid) return cudaErrorInvalidValue;
-  if (EPI == kEpiColScale && !ea.col_scale) return cudaErrorInvalidValue;
+  constexpr bool kBias = EPI == kEpiBiasGelu || EPI == kEpiBiasResid || EPI == kEpiBiasResidSS ||
+                         EPI == kEpiScaleBiasGelu || EPI == kEpiScaleBiasResid;
+  constexpr bool kResid = EPI == kEpiBiasResid || EPI == kEpiBiasResidSS ||
+                          EPI == kEpiScaleBiasResid;
+  if (EPI == kEpiBiasResidSS && (!ea.row_ss || ea.ss_stride <= 0)) return cudaErrorInvalidValue;
+  constexpr bool kScale = EPI == kEpiColScale || EPI == kEpiScaleBiasGelu ||
+                          EPI == kEpiScaleBiasResid;
+  if (kBias && !ea.bias) return cudaErrorInvalidValue;
+  if (kResid && !ea.resid) return cudaErrorInvalidValue;
+  if (kScale && !ea.col_scale) return cudaErrorInvalidValue;
   DeviceInfo* di = nullptr;
   int e = current_device_info(&di);
   if (e) return e;
@@ -368,6 +402,8 @@ int run_gemm(const bf16* A, const bf16* B, void* C, int M, int N, int K, const E
                      (!ea.resid || aligned16(ea.resid)) &&
                      (!ea.col_scale || aligned16(ea.col_scale)) && encode_fn() != nullptr;
   if (tc_ok) return launch_gemm_tc<EPI>(A, B, C, M, N, K, ea, s, di);
+  // the row sum-of-squares side output exists on the tensor-core path only
+  if constexpr (EPI == kEpiBiasResidSS) return cudaErrorNotSupported;
   return launch_gemm_simt<EPI, bf16>(A, B, C, M, N, K, ea, s);
 }
 
@@ -565,25 +601,6 @@ int run_attention(const bf16* Q, bf16* O, const KvSources& kv, int B, int H, int
   attention_simt_kernel<<<grid, 32 * warps, 0, s>>>(Q, O, kv, S_q, D, scale, causal);
   g_counters[kCntAttnSimt]++;
   return cudaGetLastError();
-}
-
-// Element-wise epilogues of the int8 MLP chain (bias+GELU on H, bias+residual on Y).
-__global__ void pkb200_bias_gelu_inplace(bf16* h, const bf16* bias, long long n, int N) {
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += stride) {
-    const float u = bf16_round(__bfloat162float(h[i]) + __bfloat162float(bias[i % N]));
-    h[i] = __float2bfloat16_rn(gelu_erf(u));
-  }
-}
-__global__ void pkb200_bias_residual_inplace(bf16* y, const bf16* bias, const bf16* x,
-                                             long long n, int N) {
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += stride) {
-    const float u = bf16_round(__bfloat162float(y[i]) + __bfloat162float(bias[i % N]));
-    y[i] = __float2bfloat16_rn(u + __bfloat162float(x[i]));
-  }
 }
 
 // out = bf16(bf16(bf16(sum_s slots[s]) + bias) + resid); the W slots are
@@ -1314,6 +1331,62 @@ int pkb200_mlp_block(const void* X, const void* gamma, const void* W1, const voi
   return pkb200_matmul_bias_residual(h, W2, b2, X, Y, M, d, ffn, stream);
 }
 
+// Per-row partial sums of squares the kEpiBiasResidSS epilogue writes: one
+// per (N tile, column half), sized for the narrowest compiled tile (128).
+static int rmsnorm_next_parts(int d) { return 2 * ((d + 127) / 128); }
+
+size_t pkb200_mlp_block_rmsnorm_next_workspace_size(int M, int d, int ffn) {
+  if (M <= 0 || d <= 0 || ffn <= 0) return 0;
+  return align_up(static_cast<size_t>(M) * d * 2) + align_up(static_cast<size_t>(M) * ffn * 2) +
+         align_up(static_cast<size_t>(M) * rmsnorm_next_parts(d) * 4);
+}
+
+int pkb200_mlp_block_rmsnorm_next(const void* X, const void* gamma, const void* W1,
+                                  const void* b1, const void* W2, const void* b2,
+                                  const void* gamma_next, void* Y, void* Yn, int M, int d, int ffn,
+                                  float eps, float eps_next, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (M < 0 || d <= 0 || ffn <= 0) return cudaErrorInvalidValue;
+  if (M == 0) return cudaSuccess;
+  if (!X || !W1 || !b1 || !W2 || !b2 || !Y || !Yn || !workspace) return cudaErrorInvalidValue;
+  if (workspace_bytes < pkb200_mlp_block_rmsnorm_next_workspace_size(M, d, ffn))
+    return cudaErrorInvalidValue;
+  const size_t xn_bytes = align_up(static_cast<size_t>(M) * d * 2);
+  const size_t h_bytes = align_up(static_cast<size_t>(M) * ffn * 2);
+  bf16* xn = b(workspace);
+  bf16* h = reinterpret_cast<bf16*>(static_cast<char*>(workspace) + xn_bytes);
+  float* row_ss = reinterpret_cast<float*>(static_cast<char*>(workspace) + xn_bytes + h_bytes);
+  int e = run_rmsnorm(cb(X), cb(gamma), xn, M, d, eps, S(stream));
+  if (e) return e;
+  e = pkb200_fused_matmul_bias_gelu(xn, W1, b1, h, M, ffn, d, stream);
+  if (e) return e;
+  const int parts = rmsnorm_next_parts(d);
+  const bool apply_ok = d % 8 == 0 && aligned16(Y) && aligned16(Yn) &&
+                        (!gamma_next || aligned16(gamma_next));
+  if (apply_ok) {
+    e = cudaMemsetAsync(row_ss, 0, static_cast<size_t>(M) * parts * 4, S(stream));
+    if (e) return e;
+    EpilogueArgs ea{};
+    ea.bias = cb(b2);
+    ea.resid = cb(X);
+    ea.ld_resid = d;
+    ea.row_ss = row_ss;
+    ea.ss_stride = parts;
+    e = run_gemm<kEpiBiasResidSS>(h, cb(W2), Y, M, d, ffn, ea, S(stream));
+    if (e == cudaSuccess) {
+      rmsnorm_apply_kernel<<<static_cast<unsigned>(M), 256, 0, S(stream)>>>(
+          cb(Y), row_ss, parts, parts, cb(gamma_next), b(Yn), d, eps_next);
+      g_counters[kCntOther]++;
+      return cudaGetLastError();
+    }
+    if (e != cudaErrorNotSupported) return e;
+  }
+  // shapes the tensor-core epilogue cannot take: GEMM2 then the row RMSNorm
+  e = pkb200_matmul_bias_residual(h, W2, b2, X, Y, M, d, ffn, stream);
+  if (e) return e;
+  return run_rmsnorm(cb(Y), cb(gamma_next), b(Yn), M, d, eps_next, S(stream));
+}
+
 int pkb200_mlp_block_int8(const void* X, const void* gamma, const int8_t* W1q,
                           const float* s1, const void* b1, const int8_t* W2q, const float* s2,
                           const void* b2, void* Y, int M, int d, int ffn, float eps,
@@ -1334,33 +1407,24 @@ int pkb200_mlp_block_int8(const void* X, const void* gamma, const int8_t* W1q,
   if (e) return e;
   e = run_rmsnorm(cb(X), cb(gamma), xn, M, d, eps, S(stream));
   if (e) return e;
-  // GEMM1: int8 matmul with per-channel scale, then bias + GELU as separate
-  // bf16 rounding steps (matmul_int8 -> bias -> gelu, each rounded).
+  // GEMM1: int8 matmul with the per-channel scale, bias and GELU in its
+  // epilogue (matmul_int8 -> bias -> gelu, each rounded to bf16 as the golden).
   e = run_int8_expand(W1q, wexp, static_cast<long long>(d) * ffn, S(stream), di);
   if (e) return e;
   EpilogueArgs ea{};
   ea.col_scale = s1;
-  e = run_gemm<kEpiColScale>(xn, wexp, h, M, ffn, d, ea, S(stream));
+  ea.bias = cb(b1);
+  e = run_gemm<kEpiScaleBiasGelu>(xn, wexp, h, M, ffn, d, ea, S(stream));
   if (e) return e;
-  // bias + GELU on H in place: reuse the SIMT elementwise path via a tiny kernel.
-  // (H = bf16(gelu(bf16(H + b1))))
-  {
-    const long long n = static_cast<long long>(M) * ffn;
-    pkb200_bias_gelu_inplace<<<grid_for(n, 256, di), 256, 0, S(stream)>>>(h, cb(b1), n, ffn);
-    g_counters[kCntOther]++;
-    e = cudaGetLastError();
-    if (e) return e;
-  }
+  // GEMM2: scale, bias and residual in its epilogue.
   e = run_int8_expand(W2q, wexp, static_cast<long long>(ffn) * d, S(stream), di);
   if (e) return e;
-  ea.col_scale = s2;
-  e = run_gemm<kEpiColScale>(h, wexp, Y, M, d, ffn, ea, S(stream));
-  if (e) return e;
-  const long long n = static_cast<long long>(M) * d;
-  pkb200_bias_residual_inplace<<<grid_for(n, 256, di), 256, 0, S(stream)>>>(b(Y), cb(b2), cb(X),
-                                                                           n, d);
-  g_counters[kCntOther]++;
-  return cudaGetLastError();
+  EpilogueArgs eb{};
+  eb.col_scale = s2;
+  eb.bias = cb(b2);
+  eb.resid = cb(X);
+  eb.ld_resid = d;
+  return run_gemm<kEpiScaleBiasResid>(h, wexp, Y, M, d, ffn, eb, S(stream));
 }
 
 int pkb200_attention_prefill(const void* Q, const void* K, const void* V, void* O, int B, int H,
@@ -1498,7 +1562,7 @@ static void cfg_out(const tuning::Config& c, int* cfg7) {
 int pkb200_gemm_select(const char* op, int M, int N, int K, int* cfg7) {
   if (!op || !cfg7) return -1;
   int epi = -1;
-  for (int e = kEpiPlain; e <= kEpiQkvScatter; ++e)
+  for (int e = kEpiPlain; e <= kEpiScaleBiasResid; ++e)  // (kind 10 shares kind 2's name)
     if (std::strcmp(op, op_name(e)) == 0) epi = e;
   if (std::strcmp(op, "fused_rmsnorm_matmul") == 0) epi = kEpiPlain;
   if (epi < 0) return -1;

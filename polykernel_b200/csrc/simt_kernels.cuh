@@ -177,6 +177,51 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_reg_kernel(
   }
 }
 
+// Second half of the RMSNorm fused behind GEMM2 (kEpiBiasResidSS): the GEMM's
+// epilogue left `parts` partial sums of squares per row in row_ss (stride
+// ss_stride); out = bf16((y / sqrt(sum/cols + eps)) * w) with the partials
+// summed in a fixed order (deterministic) and the golden's correctly rounded
+// divide (golden.py:83-90). One 256-thread CTA per row, 16-byte vectors.
+__global__ void __launch_bounds__(256) rmsnorm_apply_kernel(
+    const __nv_bfloat16* __restrict__ y, const float* __restrict__ row_ss, int ss_stride,
+    int parts, const __nv_bfloat16* __restrict__ weight, __nv_bfloat16* __restrict__ out,
+    int cols, float eps) {
+  __shared__ float rms_s;
+  const long long r = blockIdx.x;
+  if (threadIdx.x < 32) {
+    float a = 0.f;
+    for (int i = threadIdx.x; i < parts; i += 32) a += row_ss[r * ss_stride + i];
+    a = warp_sum(a);
+    if (threadIdx.x == 0) rms_s = sqrtf(a / static_cast<float>(cols) + eps);
+  }
+  __syncthreads();
+  const float rms = rms_s;
+  const uint4* yr = reinterpret_cast<const uint4*>(y + r * cols);
+  uint4* orow = reinterpret_cast<uint4*>(out + r * cols);
+  for (int c = threadIdx.x; c < (cols >> 3); c += 256) {
+    const uint4 v = yr[c];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t g4[4] = {0, 0, 0, 0};
+    if (weight) {
+      const uint4 g = reinterpret_cast<const uint4*>(weight)[c];
+      g4[0] = g.x; g4[1] = g.y; g4[2] = g.z; g4[3] = g.w;
+    }
+    uint32_t o4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16x2(w4[q]);
+      float a = __fdiv_rn(f.x, rms), b = __fdiv_rn(f.y, rms);
+      if (weight) {
+        const float2 g = unpack_bf16x2(g4[q]);
+        a *= g.x;
+        b *= g.y;
+      }
+      o4[q] = pack_bf16x2(a, b);
+    }
+    orow[c] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+}
+
 // ------------------------------------------------- residual add + RMSNorm --
 // t = bf16(x + resid) (golden.add), out = rmsnorm(t; weight, eps)
 // (golden.fused_residual_rmsnorm, golden.py:108-112). `sum_out` (nullable)
@@ -255,11 +300,16 @@ __device__ __forceinline__ float epilogue1(float acc, const EpilogueArgs& ea, lo
     return acc;
   } else if constexpr (EPI == kEpiBiasGelu) {
     return gelu_erf(bf16_round(bf16_round(acc) + __bfloat162float(ea.bias[n])));
-  } else if constexpr (EPI == kEpiBiasResid) {
+  } else if constexpr (EPI == kEpiBiasResid || EPI == kEpiBiasResidSS) {
     return bf16_round(bf16_round(acc) + __bfloat162float(ea.bias[n])) +
            __bfloat162float(ea.resid[m * ea.ld_resid + n]);
   } else if constexpr (EPI == kEpiColScale) {
     return acc * ea.col_scale[n];
+  } else if constexpr (EPI == kEpiScaleBiasGelu) {
+    return gelu_erf(bf16_round(bf16_round(acc * ea.col_scale[n]) + __bfloat162float(ea.bias[n])));
+  } else if constexpr (EPI == kEpiScaleBiasResid) {
+    return bf16_round(bf16_round(acc * ea.col_scale[n]) + __bfloat162float(ea.bias[n])) +
+           __bfloat162float(ea.resid[m * ea.ld_resid + n]);
   } else {
     return acc;
   }

@@ -259,6 +259,37 @@ def mlp_block(x, gamma, w1, b1, w2, b2, eps=1e-6, workspace=None, out=None):
     return y
 
 
+def mlp_block_rmsnorm_next(x, gamma, w1, b1, w2, b2, gamma_next=None, eps=1e-6, eps_next=1e-6,
+                           workspace=None):
+    """(Y, Yn): Y = the MLP block (the residual stream), Yn = rmsnorm(Y;
+    gamma_next) for the next layer (golden.fused_residual_rmsnorm,
+    golden.py:108-112). GEMM2's epilogue emits the per-row partial sums of
+    squares, so Yn costs one elementwise pass over Y."""
+    _req(x, "x")
+    d = x.shape[-1]
+    M = x.numel() // d
+    for t, n in ((gamma, "gamma"), (w1, "w1"), (b1, "b1"), (w2, "w2"), (b2, "b2")):
+        _req(t, n)
+    if gamma_next is not None:
+        _req(gamma_next, "gamma_next")
+        if gamma_next.numel() != d:
+            raise ValueError("gamma_next must have d elements")
+    ffn = w1.shape[1]
+    if w1.shape[0] != d or w2.shape != (ffn, d) or b1.numel() != ffn or b2.numel() != d:
+        raise ValueError("mlp_block weight shapes do not match x")
+    nbytes = lib().pkb200_mlp_block_rmsnorm_next_workspace_size(M, d, ffn)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    y = torch.empty_like(x)
+    yn = torch.empty_like(x)
+    check(lib().pkb200_mlp_block_rmsnorm_next(
+        _ptr(x), _ptr(gamma), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
+        _ptr(gamma_next) if gamma_next is not None else None, _ptr(y), _ptr(yn), M, d, ffn,
+        float(eps), float(eps_next), _ptr(workspace), workspace.numel(), _stream()),
+        "mlp_block_rmsnorm_next")
+    return y, yn
+
+
 def mlp_block_int8(x, gamma, w1q, s1, b1, w2q, s2, b2, eps=1e-6, workspace=None):
     """int8 weight-only MLP chain (quant_golden.matmul_int8 for both GEMMs)."""
     _req(x, "x")

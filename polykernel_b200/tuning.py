@@ -28,7 +28,10 @@ CONFIG_FIELDS = ("block_m", "block_n", "block_k", "num_warps", "vector_width", "
                  "shared_memory_stages")
 SMEM_LIMIT = 232448          # bytes per CTA on sm_100
 TMEM_COLUMNS = 512
-COMPILED = {(256, 4), (256, 3), (128, 4), (128, 6)}   # (block_n, stages) with a kernel
+# (block_m, block_n, stages) with a compiled kernel; block_m 256 is the CTA-pair
+# (cta_group::2) kernel: two SMs share a 256 x block_n tile, each staging half of
+# A and half of B
+COMPILED = {(128, 256, 4), (128, 256, 3), (128, 128, 4), (128, 128, 6), (256, 256, 6)}
 DEFAULT = dict(block_m=128, block_n=256, block_k=64, num_warps=10, vector_width=8, unroll=2,
                shared_memory_stages=4)
 
@@ -39,13 +42,18 @@ class SchemaError(ValueError):
 
 # ------------------------------------------------------------ config space --
 class ConfigSpace:
-    """tcgen05 GEMM configs: block_n x stages over the kernel's fixed axes."""
+    """tcgen05 GEMM configs: CTAs per tile (block_m 128: one SM; 256: a CTA
+    pair on two SMs, cta_group::2) x block_n x stages over the kernel's fixed
+    axes."""
+    block_m = (128, 256)
     block_n = (64, 128, 256)
     stages = (2, 3, 4, 5, 6, 7, 8)
 
     @staticmethod
     def smem_bytes(c):
-        stage = c["block_m"] * c["block_k"] * 2 + c["block_k"] * c["block_n"] * 2
+        # per CTA: a pair tile splits A by rows and B by columns between its CTAs
+        ctas = c["block_m"] // 128
+        stage = (c["block_m"] // ctas) * c["block_k"] * 2 + c["block_k"] * (c["block_n"] // ctas) * 2
         return c["shared_memory_stages"] * stage + 1024 + 512  # + alignment, barriers/tile ring
 
     @classmethod
@@ -54,18 +62,19 @@ class ConfigSpace:
             return "shared memory"
         if c["unroll"] * c["block_n"] > TMEM_COLUMNS:
             return "tmem columns"
-        if (c["block_n"], c["shared_memory_stages"]) not in COMPILED:
+        if (c["block_m"], c["block_n"], c["shared_memory_stages"]) not in COMPILED:
             return "no compiled variant"
         return None
 
     @classmethod
     def enumerate(cls, limit=None):
         out = []
-        for bn in cls.block_n:
-            for st in cls.stages:
-                c = dict(DEFAULT, block_n=bn, shared_memory_stages=st)
-                if cls.prune_reason(c) is None:
-                    out.append(c)
+        for bm in cls.block_m:
+            for bn in cls.block_n:
+                for st in cls.stages:
+                    c = dict(DEFAULT, block_m=bm, block_n=bn, shared_memory_stages=st)
+                    if cls.prune_reason(c) is None:
+                        out.append(c)
         return out[:limit] if limit else out
 
 
@@ -230,7 +239,8 @@ def autotune(op, M, N, K, iters=10, warmup=3, seed=0, inject_broken=False, repor
     elif op == "matmul_bias_residual":
         ref32 = ref32 + bias.float() + resid.float()
     broken_out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    candidates = [(f"block_n={c['block_n']},stages={c['shared_memory_stages']}", c, run)
+    candidates = [(f"block_m={c['block_m']},block_n={c['block_n']},"
+                   f"stages={c['shared_memory_stages']}", c, run)
                   for c in ConfigSpace.enumerate()]
     if inject_broken:
         candidates.append(("broken", None, lambda: broken_out.fill_(0.5)))

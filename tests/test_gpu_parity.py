@@ -364,3 +364,69 @@ def test_rmsnorm_wide_rows_vs_oracle(pk, cols, with_gamma):
     # any difference is one bf16 ulp (the fp32 sum of squares in another order)
     diff = np.abs(got - ref)
     assert np.all(diff <= 2.0 ** -7 * np.abs(ref) + 1e-30)
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (300, 1024, 2048), (130, 72, 136)],
+                         ids=["tiles", "ragged_m", "simt_fallback"])
+def test_mlp_block_with_next_rmsnorm_vs_golden(pk, shape):
+    """Y = MLP block and Yn = rmsnorm(Y; gamma2) (golden.fused_residual_rmsnorm
+    on the block's output and residual) with the sum of squares taken from
+    GEMM2's epilogue; Y is bit-identical to pkb200_mlp_block."""
+    M, d, ffn = shape
+    rng = np.random.default_rng(M + d)
+    X = _rand_bits(rng, (M, d)); gm = _rand_bits(rng, (d,), 0.1, 1.0)
+    W1 = _rand_bits(rng, (d, ffn), 1 / math.sqrt(d)); b1 = _rand_bits(rng, (ffn,), 0.02)
+    W2 = _rand_bits(rng, (ffn, d), 1 / math.sqrt(ffn)); b2 = _rand_bits(rng, (d,), 0.02)
+    g2 = _rand_bits(rng, (d,), 0.1, 1.0)
+    t = [t_from_bits(a) for a in (X, gm, W1, b1, W2, b2, g2)]
+    y, yn = pk.ops.mlp_block_rmsnorm_next(*t[:6], gamma_next=t[6], eps=1e-6, eps_next=1e-5)
+    y_ref_dev = pk.ops.mlp_block(*t[:6], eps=1e-6)
+    import torch
+    assert torch.equal(y, y_ref_dev)
+    # the golden composition on the device's Y (isolates the fused normalisation)
+    ref = O.fused_residual_rmsnorm(
+        O.bias(O.matmul(O.fused_matmul_bias_gelu(O.rmsnorm(F(X), F(gm), 1e-6), F(W1), F(b1)),
+                        F(W2)), F(b2)), F(X), F(g2), 1e-5)
+    on_y = O.rmsnorm(f32_from_t(y), F(g2), 1e-5)
+    got = f32_from_t(yn)
+    assert np.mean(got == on_y) >= 0.99
+    assert np.all(np.abs(got - on_y) <= 2.0 ** -7 * np.abs(on_y) + 1e-30)
+    print(shape, check_parity(got, ref, min_exact=0.97))
+    assert pk.device_error() == 0
+
+
+def test_next_rmsnorm_timing_vs_unfused(pk):
+    """Informational: GEMM2 + the standalone row RMSNorm against the fused
+    epilogue + apply pass, config-2 shape."""
+    import time
+
+    import torch
+    M, d, ffn = 2048, 4096, 16384
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(M, d, device="cuda", generator=g).bfloat16()
+    gm = (1 + 0.1 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+    w1 = (torch.randn(d, ffn, device="cuda", generator=g) / 64).bfloat16()
+    b1 = (0.02 * torch.randn(ffn, device="cuda", generator=g)).bfloat16()
+    w2 = (torch.randn(ffn, d, device="cuda", generator=g) / 128).bfloat16()
+    b2 = (0.02 * torch.randn(d, device="cuda", generator=g)).bfloat16()
+
+    def unfused():
+        y = pk.ops.mlp_block(x, gm, w1, b1, w2, b2)
+        return pk.ops.rmsnorm(y, gm, 1e-6)
+
+    def fused():
+        return pk.ops.mlp_block_rmsnorm_next(x, gm, w1, b1, w2, b2, gm)[1]
+
+    res = {}
+    for name, fn in (("unfused", unfused), ("fused", fused)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        res[name] = (time.perf_counter() - t0) / 10 * 1e3
+    print("ms", res)
+    # the same normalisation up to the order of the fp32 sum of squares
+    assert (unfused() == fused()).float().mean().item() >= 0.99

@@ -60,8 +60,8 @@ def test_c_loader_rejects_malformed_json(tmp_path):
 
 def test_config_space_pruning():
     cfgs = T.ConfigSpace.enumerate()
-    pairs = {(c["block_n"], c["shared_memory_stages"]) for c in cfgs}
-    assert pairs == T.COMPILED
+    triples = {(c["block_m"], c["block_n"], c["shared_memory_stages"]) for c in cfgs}
+    assert triples == T.COMPILED
     assert T.ConfigSpace.prune_reason(dict(T.DEFAULT, shared_memory_stages=5)) in (
         "shared memory", "no compiled variant")
     assert T.ConfigSpace.prune_reason(dict(T.DEFAULT, shared_memory_stages=8)) == "shared memory"
@@ -142,8 +142,8 @@ def test_autotune_cache_roundtrip_on_gpu(cuda, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("bn,stages", sorted(T.COMPILED))
-def test_every_compiled_variant_matches_default(cuda, bn, stages):
+@pytest.mark.parametrize("bm,bn,stages", sorted(T.COMPILED))
+def test_every_compiled_variant_matches_default(cuda, bm, bn, stages):
     import torch
     import polykernel_b200 as pk
     g = torch.Generator(device="cuda").manual_seed(5)
@@ -153,12 +153,13 @@ def test_every_compiled_variant_matches_default(cuda, bn, stages):
         bias = torch.randn(N, device="cuda", generator=g).bfloat16()
         ref = pk.ops.fused_matmul_bias_gelu(a, b, bias)
         assert lib().pkb200_set_gemm_config(
-            T._cfg_array(dict(T.DEFAULT, block_n=bn, shared_memory_stages=stages))) == 0
+            T._cfg_array(dict(T.DEFAULT, block_m=bm, block_n=bn,
+                              shared_memory_stages=stages))) == 0
         try:
             out = pk.ops.fused_matmul_bias_gelu(a, b, bias)
         finally:
             lib().pkb200_set_gemm_config(None)
-        assert torch.equal(out, ref), (bn, stages, M, N, K)
+        assert torch.equal(out, ref), (bm, bn, stages, M, N, K)
     assert pk.device_error() == 0
 
 
@@ -174,7 +175,8 @@ def test_autotune_rejects_injected_broken_variant(cuda):
     assert broken and not broken[0]["validated"]
     assert broken[0]["time_ms"] <= min(r["time_ms"] for r in report)
     assert len(entries) == 1 and entries[0]["validated"]
-    assert (entries[0]["best"]["block_n"], entries[0]["best"]["shared_memory_stages"]) in T.COMPILED
+    best = entries[0]["best"]
+    assert (best["block_m"], best["block_n"], best["shared_memory_stages"]) in T.COMPILED
 
 
 def test_cli_enumerate_validate_show(tmp_path, capsys):
@@ -182,7 +184,8 @@ def test_cli_enumerate_validate_show(tmp_path, capsys):
     assert T.main(["enumerate", "--limit", "2"]) == 0
     lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.strip()]
     assert len(lines) == 2
-    assert all((_json.loads(ln)["block_n"], _json.loads(ln)["shared_memory_stages"]) in T.COMPILED
+    assert all((_json.loads(ln)["block_m"], _json.loads(ln)["block_n"],
+                _json.loads(ln)["shared_memory_stages"]) in T.COMPILED
                for ln in lines)
     doc = T.merge({"version": 1, "entries": []},
                   [T.entry("sm_100", "matmul", 256, 512, 1024, T.DEFAULT, 0.01, True,
