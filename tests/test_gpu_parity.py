@@ -17,7 +17,8 @@ import pytest
 
 from oracle import golden_np as O
 from oracle import metrics as Mx
-from tests.helpers import (bits_from_t, check_attention, check_gate, check_parity, f32_from_t,
+from tests.helpers import (bits_from_t, check_attention, check_chain, check_gate, check_parity,
+                           f32_from_t,
                            t_from_bits)
 
 pytestmark = pytest.mark.gpu
@@ -391,7 +392,9 @@ def test_mlp_block_with_next_rmsnorm_vs_golden(pk, shape):
     got = f32_from_t(yn)
     assert np.mean(got == on_y) >= 0.99
     assert np.all(np.abs(got - on_y) <= 2.0 ** -7 * np.abs(on_y) + 1e-30)
-    print(shape, check_parity(got, ref, min_exact=0.97))
+    # against the golden composition from X: the bf16 chain's one-ulp flips in
+    # Y propagate (the rule of the full-size chain tests)
+    print(shape, check_chain(got, ref))
     assert pk.device_error() == 0
 
 
