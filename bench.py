@@ -761,6 +761,7 @@ PROFILE_CASES = {
     "attn": "attention_prefill, BASELINE config 3 (B=4, H=32, S=2048, D=128, causal)",
     "attn_b1": "attention_prefill, config 3 with B=1 (the ncu capture case)",
     "gemm1c5": "fused_matmul_bias_gelu at config-5 GEMM1 shape with M=4096 (d=8192, ffn=28672)",
+    "gemm1c5_pair": "gemm1c5 on the CTA-pair (cta_group::2) GEMM variant",
     "gemm2c5": "matmul + bias + residual (mlp GEMM2 epilogue) at config-5 GEMM2 shape, M=4096",
     "gemm": "plain matmul 2048 x 4096 x 16384 (config-2 GEMM1 shape)",
     "rmsnorm_c5": "rmsnorm with gamma over config-5 X (16384 x 8192)",
@@ -781,7 +782,11 @@ def run_profile_case(which):
         k, v = torch.randn_like(q), torch.randn_like(q)
         for _ in range(3):
             pk.ops.attention_prefill(q, k, v, True)
-    elif which == "gemm1c5":
+    elif which in ("gemm1c5", "gemm1c5_pair"):
+        if which == "gemm1c5_pair":
+            from polykernel_b200._lib import check, lib
+            check(lib().pkb200_set_gemm_config((ctypes.c_int * 7)(256, 256, 64, 10, 8, 2, 6)),
+                  "set_gemm_config")
         a = torch.randn(4096, 8192, device=dev).bfloat16()
         b = (torch.randn(8192, 28672, device=dev) / 90).bfloat16()
         bias = (0.02 * torch.randn(28672, device=dev)).bfloat16()
