@@ -176,7 +176,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int NUM_THREADS = 320;            // 2 control warps + 8 epilogue warps
 constexpr int EPI_THREADS = 256;
-constexpr int GROUP_M = 16;                 // rasterisation group (L2 reuse)
+constexpr int GROUP_ROWS = 2048;            // rasterisation group: output rows sharing W panels in L2
 constexpr int SCHED_DEPTH = 8;              // tile ids in flight producer -> consumers
 // Tunable per launch (the tuning cache's block_n / shared_memory_stages):
 // tile width BN in {128, 256} and pipeline depth STAGES.
@@ -195,11 +195,12 @@ constexpr int smem_bytes_peer(int bn, int stages) {
 constexpr int kMaxSmem = 232448;                    // 227 KB per CTA on sm_100
 }  // namespace gemm
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
-  const int per_group = gemm::GROUP_M * tiles_n;
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& mb,
+                                            int& nb) {
+  const int per_group = group_m * tiles_n;
   const int g = t / per_group;
-  const int first_m = g * gemm::GROUP_M;
-  const int gm = min(gemm::GROUP_M, tiles_m - first_m);
+  const int first_m = g * group_m;
+  const int gm = min(group_m, tiles_m - first_m);
   const int local = t - g * per_group;
   mb = first_m + local % gm;
   nb = local / gm;
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, void* __restrict__ C, long long ldc,
                    int M, int N, int K, EpilogueArgs ea, int* err,
-                   const __grid_constant__ PeerMaps peer_maps, int* tile_counter) {
+                   const __grid_constant__ PeerMaps peer_maps, int* tile_counter, int group_m) {
   using gemm::BM;
   using gemm::BK;
   using gemm::EPI_THREADS;
@@ -296,7 +297,7 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
         const int next = tile_counter ? static_cast<int>(gridDim.x) + atomicAdd(tile_counter, 1)
                                       : t + static_cast<int>(gridDim.x);
         int mb, nb;
-        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        tile_coords(t, tiles_m, tiles_n, group_m, mb, nb);
         t = next;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag, kErrTimeoutProducer)) {
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       }
       if (t < 0) break;
       int mb, nb;
-      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      tile_coords(t, tiles_m, tiles_n, group_m, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, abort_flag, kErrTimeoutEpilogue)) break;

@@ -113,7 +113,8 @@ template <int EPI, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
                     const __grid_constant__ CUtensorMap map_b, void* __restrict__ C,
-                    long long ldc, int M, int N, int K, EpilogueArgs ea, int* err) {
+                    long long ldc, int M, int N, int K, EpilogueArgs ea, int* err,
+                    int group_m) {
   using namespace gemm2;
   static_assert(EPI != kEpiPeerStoreF32 && EPI != kEpiQkvScatter, "single-SM kernel only");
   static_assert(smem_bytes(STAGES) <= gemm::kMaxSmem, "pipeline does not fit");
@@ -170,7 +171,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 
       bool ok = true;
       for (int t = cluster; t < num_tiles && ok; t += clusters) {
         int mb, nb;
-        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        tile_coords(t, tiles_m, tiles_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag, kErrTimeoutProducer)) {
             ok = false;
@@ -238,7 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 
     int local = 0;
     for (int t = cluster; t < num_tiles; t += clusters, ++local) {
       int mb, nb;
-      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      tile_coords(t, tiles_m, tiles_n, group_m, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err, abort_flag, kErrTimeoutEpilogue)) break;

@@ -9,6 +9,7 @@
 #include <chrono>
 #include <thread>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <sstream>
@@ -272,6 +273,21 @@ int next_tile_counter(int dev, int** out) {
   return cudaSuccess;
 }
 
+// Tile rows of one rasterisation group: tiles are numbered down a group of
+// GROUP_ROWS output rows before moving one column panel right, so the A rows
+// of a group (GROUP_ROWS x K bf16, 32 MB at K = 8192) stay in L2 while the
+// weight panels stream past once per group. PKB200_GEMM_GROUP_ROWS overrides
+// the row count (tuning experiments).
+int group_tiles(int tile_rows) {
+  static const int rows = [] {
+    const char* v = std::getenv("PKB200_GEMM_GROUP_ROWS");
+    const int r = v ? std::atoi(v) : 0;
+    return r > 0 ? r : gemm::GROUP_ROWS;
+  }();
+  const int g = rows / tile_rows;
+  return g > 0 ? g : 1;
+}
+
 template <int EPI, int BN, int STAGES>
 int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N,
                         int K, const EpilogueArgs& ea, cudaStream_t s, DeviceInfo* di,
@@ -296,7 +312,7 @@ int launch_gemm_variant(const CUtensorMap& ma, const CUtensorMap& mb, void* C, i
   }
   gemm_tc_kernel<EPI, BN, STAGES><<<grid, gemm::NUM_THREADS, smem, s>>>(
       ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err, peer ? *peer : kNoPeers,
-      counter);
+      counter, group_tiles(gemm::BM));
   g_counters[kCntGemmTc]++;
   return cudaGetLastError();
 }
@@ -309,13 +325,33 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int 
                                      smem))
     return e;
   const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+  // The static tile schedule assumes every launched pair is resident at once:
+  // a pair that only starts when another finishes would run a second, serial
+  // share of the tiles. Launch no more pairs than the device can co-schedule.
+  static std::atomic<int> max_pairs[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (max_pairs[dev].load() == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(di->sms & ~1));
+    cfg.blockDim = dim3(gemm2::NUM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<EPI, STAGES>, &cfg) != cudaSuccess ||
+        n <= 0) {
+      (void)cudaGetLastError();
+      n = di->sms / 2;
+    }
+    max_pairs[dev].store(n);
+  }
   long long grid = di->sms & ~1;  // whole CTA pairs
+  if (grid > 2LL * max_pairs[dev].load()) grid = 2LL * max_pairs[dev].load();
   const int cap = g_gemm_max_ctas.load();
   if (cap > 0 && cap < grid) grid = cap & ~1;
   if (2 * tiles < grid) grid = 2 * tiles;
   if (grid < 2) grid = 2;
   gemm_tc2_kernel<EPI, STAGES><<<static_cast<unsigned>(grid), gemm2::NUM_THREADS, smem, s>>>(
-      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err);
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err, group_tiles(2 * gemm2::BM));
   g_counters[kCntGemmTc]++;
   return cudaGetLastError();
 }

@@ -59,3 +59,22 @@ def test_noalloc_rejects_oversize(cuda):
     w = torch.zeros(K, N, device="cuda", dtype=torch.bfloat16)
     out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
     assert _call(lib, "pkb200_fused_rmsnorm_matmul_noalloc", x, w, None, out, 1e-5) == 1
+
+
+def test_noalloc_at_the_scratch_limit(cuda):
+    """M*K exactly equal to the scratch array's 8,388,608 elements is accepted
+    and gives the allocating entry point's output."""
+    import torch
+    import polykernel_b200 as pk
+    lib = pk.lib()
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    M, K, N = 2048, 4096, 64
+    x = torch.randn(M, K, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (torch.randn(K, N, device="cuda", generator=gen) / K ** 0.5).to(torch.bfloat16)
+    ref = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    assert _call(lib, "pkb200_fused_rmsnorm_matmul", x, w, None, ref, 1e-6) == 0
+    assert _call(lib, "pkb200_fused_rmsnorm_matmul_noalloc", x, w, None, out, 1e-6) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert pk.device_error() == 0
