@@ -441,6 +441,10 @@ def run_gpu_arm(args):
     barrier()
     k_ms = [a.elapsed_time(b) for a, b in ev]
     gemm1_ms = statistics.mean(k_ms)
+    _cfg7 = (ctypes.c_int * 7)()
+    pk.lib().pkb200_last_gemm_config(_cfg7)
+    g1_kernel = ("gemm_tc2_kernel<bias+GELU> (MLP GEMM1, CTA pair, 256x256 tiles)" if _cfg7[0] == 256
+                 else "gemm_tc_kernel<bias+GELU> (MLP GEMM1, 128x256 tiles)")
     # Attention alone (same shapes), for its own roofline figure: once right
     # after the GEMMs (clocks still held down by the MLP's power draw, as in the
     # step) and once after 2 s idle (burst clocks, the kernel's own speed,
@@ -726,7 +730,7 @@ def run_gpu_arm(args):
                       "attention_timed": "alone, after 2 s idle (burst clocks)",
                       "attention_ms_right_after_mlp": attn_after_mlp_ms,
                       "attention_frac_of_peak": a_tflops / burst},
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel<bias+GELU> (MLP GEMM1)",
+            "roofline": {"bound": "tensor", "kernel": g1_kernel,
                          "achieved": g1_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": g1_tflops / peak,
                          "peak_kind": f"{kind} bf16 burst (GEMM1 timed alone)",

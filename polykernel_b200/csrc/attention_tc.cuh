@@ -7,8 +7,8 @@
 // causal (attention_prefill.cu:103), softmax in fp32, P.V accumulated in fp32,
 // one bf16 rounding of O. Rows that see no key produce 0 (attention_prefill.cu:154).
 //
-// One CTA per (128-query tile, batch*head), longest tiles first. Roles (512
-// threads):
+// One CTA per (128-query tile, batch*head); blocks run in groups of heads,
+// longest tiles first within a group. Roles (448 threads):
 //   warps 0-7  softmax. Warp w of group h (warps 4h..4h+3) handles key half h
 //              (64 keys) of every key tile for the query rows of TMEM lane
 //              quarter w%4; thread r owns query row r (= TMEM lane r). It
@@ -21,30 +21,32 @@
 //              arithmetic so the SFU pipe only runs exp2), where the P.V MMAs
 //              read it as their A operand. Per key tile group 0 hands the row's
 //              rescale factor (2^(m_old - m_new)) to the correction warps.
-//   warps 8-11 correction. Each key tile's P.V lands in a fresh TMEM
-//              accumulator Ot (16 MMA steps deep); thread r folds it into the
-//              running O of row r with fp32 FMAs, O = O * alpha + Ot, in TMEM.
-//              At the end it normalises O by the row sum and stores it.
-//   warp 12    TMA producer: the Q tile once; K and V tiles (128 keys) through
-//              2-deep rings. For the append entry point, the CTA whose query
-//              tile matches a tile of new rows also writes those K/V tiles
-//              from shared memory into the cache with TMA stores, so the
-//              append costs no extra HBM read.
-//   warp 13    TMEM owner + single-thread MMA issuer. Per key tile j: S(j+1)
-//              into the other S buffer (once P.V(j-1) has read it), then
-//              P.V(j) = P_hi.V + P_lo.V into Ot (once the correction warps have
-//              drained Ot). So the tensor core computes S(j+1) while the
-//              softmax works on S(j), and P.V(j) while the softmax works on
-//              S(j+1).
-//   warps 14-15 V converter: each V tile is rewritten in place in shared
-//              memory from bf16 to fp16 (same layout, same swizzle) before the
-//              P.V MMAs read it. Every bf16 value in [2^-17, 65280] is exactly
-//              an fp16 value. A tile that holds a value of magnitude >= 2^16
-//              (or inf), or a warp's share of a tile whose values are all
-//              below 2^-6 (where values below 2^-17 would lose bits), marks the
-//              CTA; such a CTA
+//   warps 8-11 correction and V conversion. Each key tile's P.V lands in a
+//              fresh TMEM accumulator Ot (16 MMA steps deep); thread r folds
+//              it into the running O of row r with fp32 FMAs,
+//              O = O * alpha + Ot, in TMEM. While the tensor core runs P.V(j)
+//              these warps rewrite V(j+1) in place in shared memory from bf16
+//              to fp16 (same layout, same swizzle) for the next P.V. Every
+//              bf16 value in [2^-17, 65280] is exactly an fp16 value. A tile
+//              that holds a value of magnitude >= 2^16 (or inf), or a warp's
+//              share of a tile whose values are all below 2^-6 (where values
+//              below 2^-17 would lose bits), marks the CTA; such a CTA
 //              recomputes its query rows with the exact SIMT row routine after
 //              the tensor-core pass, so the result never depends on fp16 range.
+//              At the end they normalise O by the row sum and store it.
+//   warp 12    TMA producer: the Q tile once; K tiles (128 keys) through a
+//              2-deep ring and V tiles through a 3-deep ring, each load issued
+//              as soon as its slot frees. For the append entry point, the CTA
+//              whose query tile matches a tile of new rows also writes those
+//              K/V tiles from shared memory into the cache with TMA stores, so
+//              the append costs no extra HBM read.
+//   warp 13    TMEM owner + MMA issuer (the whole warp runs the loop; one
+//              elected lane issues). Per key tile j: S(j+1) into the other S
+//              buffer (once P.V(j-1) has read it), then
+//              P.V(j) = P_hi.V + P_lo.V into Ot (once pv_ready(j) says P(j),
+//              fp16 V(j) and a drained Ot are in place). So the tensor core
+//              computes S(j+1) while the softmax works on S(j), and P.V(j)
+//              while the softmax works on S(j+1).
 //
 // Numerics: scores are fp32 (bf16 Q.K on tensor cores), P is fp32 from the
 // SFU exp2 and enters P.V as fp16 hi+lo (relative error ~2^-21), V enters as
@@ -75,16 +77,22 @@ constexpr int BN = 128;           // keys per tile
 constexpr int KST = 2;            // K pipeline stages
 constexpr int VST = 3;            // V pipeline stages (TMA, then fp16 conversion)
 constexpr int NUM_THREADS = 512;
-constexpr int kConvThreads = 64;  // warps 14-15
-constexpr int kWarpProducer = 12, kWarpMma = 13, kWarpConv0 = 14;
+constexpr int kConvThreads = 128;  // the correction warps 8-11 convert V
+constexpr int kWarpProducer = 12, kWarpMma = 13;  // warps 14-15 idle
+// Registers per thread by warpgroup (launch: 512 x 128): softmax warpgroups 0
+// and 1 keep 128; the correction warpgroup holds its rows' O (D fp32) in
+// registers; warpgroup 3 (producer, MMA issuer) needs few.
+// 2 x 128 + kRegsCorrection + kRegsControl = 4 x 128.
+constexpr int kRegsCorrection = 176;
+constexpr int kRegsControl = 80;
+static_assert(kRegsCorrection + kRegsControl == 2 * 128, "register split must fit the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Probabilities are formed as 2^7 * p: with the stale-max threshold p <= 2^8,
 // so 2^7 * p <= 2^15 stays inside fp16's range while the values that would
 // fall into fp16's subnormal range shrink by 2^7. The row sum carries the same
 // factor, so O = sum(P.V) / sum(P) is unchanged.
 constexpr float kPScaleLog2 = 7.0f;
-constexpr uint32_t kColOt = 256;  // per-key-tile P.V accumulator
-constexpr uint32_t kColO = 384;   // running O
+constexpr uint32_t kColOt = 256;  // per-key-tile P.V accumulators Ot[j & 1]: 256, 384
 
 template <int D>
 struct Layout {
@@ -113,6 +121,7 @@ struct AttnTcParams {
   int causal;
   int append;     // 1: write source-B tiles into the cache maps
   int num_qtiles;
+  int head_group;  // heads per scheduling group (block order below)
   __nv_bfloat16* O;
   int* err;
   // exact fallback (rows of CTAs whose V tiles fp16 cannot carry exactly)
@@ -172,14 +181,17 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   uint64_t* k_empty = k_full + KST;       // [KST]
   uint64_t* v_full = k_empty + KST;       // [VST] TMA landed (bf16)
   uint64_t* v_empty = v_full + VST;       // [VST]
-  uint64_t* v_conv = v_empty + VST;       // [VST] converted to fp16
-  uint64_t* s_full = v_conv + VST;        // [2]  S(j) in S/P buffer j&1
-  uint64_t* p_full = s_full + 2;          // [2]  P(j) written over it
-  uint64_t* alpha_full = p_full + 2;      // [2]  rescale factors of tile j
+  // pv_ready[j % VST]: everything P.V(j) reads is in place: P(j) written
+  // over S(j) (softmax warps), V(j) converted to fp16 and Ot drained of
+  // P.V(j-1) (correction warps). One barrier, so the MMA warp polls once.
+  // No role can arrive for tile j+VST before tile j's phase completes: each
+  // such arrival needs P.V(j+1) or later issued.
+  uint64_t* pv_ready = v_empty + VST;     // [VST]
+  uint64_t* s_full = pv_ready + VST;      // [2]  S(j) in S/P buffer j&1
+  uint64_t* alpha_full = s_full + 2;      // [2]  rescale factors of tile j
   uint64_t* alpha_empty = alpha_full + 2; // [2]
-  uint64_t* pv_done = alpha_empty + 2;    // P.V(j) in Ot
-  uint64_t* ot_free = pv_done + 1;        // Ot drained into O
-  uint64_t* l_ready = ot_free + 1;        // row sums in l_s
+  uint64_t* pv_done = alpha_empty + 2;    // [2]  P.V(j) in Ot[j&1]
+  uint64_t* l_ready = pv_done + 2;        // row sums in l_s
   uint64_t* v_stored = l_ready + 1;       // appended V tile read out of smem
   uint64_t* pair_bar = v_stored + 1;      // [4] the two softmax warps of a lane quarter
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
@@ -188,10 +200,20 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  // One-dimensional grid ordered longest query tiles first across all heads,
-  // so the block scheduler fills the SMs longest-job-first.
-  const int bh = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.BH));
-  const int qt = p.num_qtiles - 1 - static_cast<int>(blockIdx.x / static_cast<unsigned>(p.BH));
+  // One-dimensional grid in groups of head_group heads; within a group the
+  // longest query tiles come first across its heads, so the block scheduler
+  // fills the SMs longest-job-first while the CTAs in flight share the K/V
+  // of a few heads in L2.
+  int bh, qt;
+  {
+    const int blk = static_cast<int>(blockIdx.x);
+    const int per_group = p.head_group * p.num_qtiles;
+    const int g = blk / per_group;
+    const int gsize = min(p.head_group, p.BH - g * p.head_group);
+    const int r = blk - g * per_group;
+    bh = g * p.head_group + r % gsize;
+    qt = p.num_qtiles - 1 - r / gsize;
+  }
   const int nt = attn_tiles_for(p, qt);
 
   if (threadIdx.x == 0) {
@@ -203,16 +225,15 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
     for (int i = 0; i < VST; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&v_conv[i], kConvThreads);
+      mbar_init(&pv_ready[i], 2 * BM + BM);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2 * BM);
       mbar_init(&alpha_full[i], BM);
       mbar_init(&alpha_empty[i], BM);
     }
-    mbar_init(pv_done, 1);
-    mbar_init(ot_free, BM);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     mbar_init(l_ready, 2 * BM);
     mbar_init(v_stored, 1);
     for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
@@ -229,140 +250,141 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWarpProducer) {
-    if (lane == 0 && nt > 0) {
-      // -------------------------------------------------------- producer --
-      tma_prefetch_desc(&map_q);
-      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
-#pragma unroll
-      for (int c = 0; c < L::DBOX; ++c)
-        tma_load_3d(smem + L::OFF_Q + c * (BM * 128), &map_q, q_full, c * 64, qt * BM, bh);
-      for (int j = 0; j < nt; ++j) {
-        const bool from_a = j < p.tiles_a;
-        const int row0 = from_a ? j * BN : (j - p.tiles_a) * BN;
-        const CUtensorMap* mk = from_a ? &map_ka : &map_kb;
-        const CUtensorMap* mv = from_a ? &map_va : &map_vb;
-        const int ks = j % KST, vs = j % VST;
-        const uint32_t kph = (j / KST) & 1, vph = (j / VST) & 1;
-        uint8_t* sk = smem + L::OFF_K + ks * L::KV_BYTES;
-        uint8_t* sv = smem + L::OFF_V + vs * L::KV_BYTES;
-        // V first: its conversion sits between the load and the P.V MMAs.
-        if (!mbar_wait(&v_empty[vs], vph ^ 1, p.err, abort_flag, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&v_full[vs], L::KV_BYTES);
+  if (warp >= kWarpProducer) {
+    setmaxnreg_dec<kRegsControl>();
+    if (warp == kWarpProducer) {
+      if (lane == 0 && nt > 0) {
+        // -------------------------------------------------------- producer --
+        tma_prefetch_desc(&map_q);
+        mbar_arrive_expect_tx(q_full, L::Q_BYTES);
 #pragma unroll
         for (int c = 0; c < L::DBOX; ++c)
-          tma_load_3d(sv + c * (BN * 128), mv, &v_full[vs], c * 64, row0, bh);
-        if (!mbar_wait(&k_empty[ks], kph ^ 1, p.err, abort_flag, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&k_full[ks], L::KV_BYTES);
+          tma_load_3d(smem + L::OFF_Q + c * (BM * 128), &map_q, q_full, c * 64, qt * BM, bh);
+        // K and V tiles are issued independently, each as soon as its ring
+        // slot is released (a K slot frees when S(j) completes, a V slot when
+        // P.V(j) does), so a K load never queues behind a V slot. V(j) is
+        // issued only after K(j).
+        int jk = 0, jv = 0;
+        bool ok = true;
+        long long t_idle = clock64();
+        while (ok && jv < nt) {
+          bool progressed = false;
+          if (jk < nt && mbar_test_wait(&k_empty[jk % KST], ((jk / KST) & 1) ^ 1)) {
+            const int row0 = jk < p.tiles_a ? jk * BN : (jk - p.tiles_a) * BN;
+            uint8_t* sk = smem + L::OFF_K + (jk % KST) * L::KV_BYTES;
+            mbar_arrive_expect_tx(&k_full[jk % KST], L::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < L::DBOX; ++c)
-          tma_load_3d(sk + c * (BN * 128), mk, &k_full[ks], c * 64, row0, bh);
-        if (attn_append_tile(p, j, qt)) {
-          // Write this tile of new rows into the cache (rows n_a + row0 ...),
-          // V before the converter rewrites it as fp16.
-          if (!mbar_wait(&k_full[ks], kph, p.err, abort_flag, kErrTimeoutProducer)) break;
+            for (int c = 0; c < L::DBOX; ++c)
+              tma_load_3d(sk + c * (BN * 128), jk < p.tiles_a ? &map_ka : &map_kb, &k_full[jk % KST],
+                          c * 64, row0, bh);
+            if (attn_append_tile(p, jk, qt)) {
+              // Write this tile of new rows into the cache (rows n_a + row0 ...)
+              // before the slot can be reused.
+              if (!mbar_wait(&k_full[jk % KST], (jk / KST) & 1, p.err, abort_flag,
+                             kErrTimeoutProducer))
+                break;
 #pragma unroll
-          for (int c = 0; c < L::DBOX; ++c)
-            tma_store_3d(&map_kc_store, sk + c * (BN * 128), c * 64, p.n_a + row0, bh);
-          if (!mbar_wait(&v_full[vs], vph, p.err, abort_flag, kErrTimeoutProducer)) break;
+              for (int c = 0; c < L::DBOX; ++c)
+                tma_store_3d(&map_kc_store, sk + c * (BN * 128), c * 64, p.n_a + row0, bh);
+              bulk_commit_group();
+              bulk_wait_group_read0();
+            }
+            ++jk;
+            progressed = true;
+          }
+          if (jv < jk && mbar_test_wait(&v_empty[jv % VST], ((jv / VST) & 1) ^ 1)) {
+            const int j = jv;
+            const int row0 = j < p.tiles_a ? j * BN : (j - p.tiles_a) * BN;
+            const int vs = j % VST;
+            uint8_t* sv = smem + L::OFF_V + vs * L::KV_BYTES;
+            mbar_arrive_expect_tx(&v_full[vs], L::KV_BYTES);
 #pragma unroll
-          for (int c = 0; c < L::DBOX; ++c)
-            tma_store_3d(&map_vc_store, sv + c * (BN * 128), c * 64, p.n_a + row0, bh);
-          bulk_commit_group();
-          bulk_wait_group_read0();
-          mbar_arrive(v_stored);
+            for (int c = 0; c < L::DBOX; ++c)
+              tma_load_3d(sv + c * (BN * 128), j < p.tiles_a ? &map_va : &map_vb, &v_full[vs], c * 64,
+                          row0, bh);
+            if (attn_append_tile(p, j, qt)) {
+              // The appended V tile goes to the cache before the correction
+              // warps rewrite it as fp16 (they wait for v_stored).
+              if (!mbar_wait(&v_full[vs], (j / VST) & 1, p.err, abort_flag, kErrTimeoutProducer)) break;
+#pragma unroll
+              for (int c = 0; c < L::DBOX; ++c)
+                tma_store_3d(&map_vc_store, sv + c * (BN * 128), c * 64, p.n_a + row0, bh);
+              bulk_commit_group();
+              bulk_wait_group_read0();
+              mbar_arrive(v_stored);
+            }
+            ++jv;
+            progressed = true;
+          }
+          if (progressed) {
+            t_idle = clock64();
+          } else if (*abort_flag) {
+            ok = false;
+          } else if (clock64() - t_idle > kSpinLimitCycles) {
+            atomicCAS(p.err, 0, kErrTimeoutProducer);
+            *abort_flag = 1;
+            ok = false;
+          }
         }
+        bulk_wait_group0();
       }
-      bulk_wait_group0();
-    }
-  } else if (warp == kWarpMma) {
-    if (lane == 0 && nt > 0) {
-      // ------------------------------------------------------ MMA issuer --
-      constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
-      constexpr uint32_t idesc_o = make_idesc_f16(BM, D, false, true);
-      const uint32_t q_addr = smem_u32(smem + L::OFF_Q);
-      auto issue_s = [&](int j) {
-        const uint32_t k_addr = smem_u32(smem + L::OFF_K + (j % KST) * L::KV_BYTES);
+    } else if (warp == kWarpMma) {
+      if (nt > 0) {
+        // ------------------------------------------------------ MMA issuer --
+        // The whole warp runs this loop (warp-uniform values); one elected lane
+        // issues each MMA and commit.
+        constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
+        constexpr uint32_t idesc_o = make_idesc_f16(BM, D, false, true);
+        const uint32_t q_addr = smem_u32(smem + L::OFF_Q);
+        auto issue_s = [&](int j) {
+          const uint32_t k_addr = smem_u32(smem + L::OFF_K + (j % KST) * L::KV_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t ad = make_sw128_desc(q_addr + off, 16, 1024);
-          const uint64_t bd = make_sw128_desc(k_addr + off, 16, 1024);
-          tc_mma_f16(tmem + (j & 1) * BN, ad, bd, idesc_s, kk != 0);
-        }
-        tc_commit(&k_empty[j % KST]);
-        tc_commit(&s_full[j & 1]);
-      };
-      auto issue_pv = [&](int j) {
-        const uint32_t v_addr = smem_u32(smem + L::OFF_V + (j % VST) * L::KV_BYTES);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+            const uint64_t ad = make_sw128_desc(q_addr + off, 16, 1024);
+            const uint64_t bd = make_sw128_desc(k_addr + off, 16, 1024);
+            tc_mma_f16_warp(tmem + (j & 1) * BN, ad, bd, idesc_s, kk != 0);
+          }
+          tc_commit_warp(&k_empty[j % KST]);
+          tc_commit_warp(&s_full[j & 1]);
+        };
+        auto issue_pv = [&](int j) {
+          const uint32_t v_addr = smem_u32(smem + L::OFF_V + (j % VST) * L::KV_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, BN * 128, 1024);
-          const uint32_t a_hi = tmem + (j & 1) * BN + (kk >> 2) * 64 + (kk & 3) * 8;
-          tc_mma_f16_tmem_a(tmem + kColOt, a_hi, bd, idesc_o, kk != 0);
-          tc_mma_f16_tmem_a(tmem + kColOt, a_hi + 32, bd, idesc_o, 1);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, BN * 128, 1024);
+            const uint32_t a_hi = tmem + (j & 1) * BN + (kk >> 2) * 64 + (kk & 3) * 8;
+            tc_mma_f16_tmem_a_warp(tmem + kColOt + (j & 1) * 128, a_hi, bd, idesc_o, kk != 0);
+            tc_mma_f16_tmem_a_warp(tmem + kColOt + (j & 1) * 128, a_hi + 32, bd, idesc_o, 1);
+          }
+          tc_commit_warp(&v_empty[j % VST]);
+          tc_commit_warp(&pv_done[j & 1]);
+        };
+        // every wait is taken by the whole warp, so the warp stays converged
+        auto wait = [&](uint64_t* bar, uint32_t parity) {
+          return __all_sync(0xffffffffu,
+                            mbar_wait_poll(bar, parity, p.err, abort_flag, kErrTimeoutMma));
+        };
+        bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0);
         }
-        tc_commit(&v_empty[j % VST]);
-        tc_commit(pv_done);
-      };
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag, kErrTimeoutMma);
-      if (ok) ok = mbar_wait(&k_full[0], 0, p.err, abort_flag, kErrTimeoutMma);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; j < nt && ok; ++j) {
-        if (j + 1 < nt) {
-          // S(j+1) goes into the buffer that held P(j-1): P.V(j-1) must be done.
-          ok = mbar_wait(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1, p.err, abort_flag,
-                         kErrTimeoutMma);
-          if (ok && j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1, p.err, abort_flag, kErrTimeoutMma);
+        for (int j = 0; j < nt && ok; ++j) {
+          if (j + 1 < nt) {
+            // S(j+1) goes into the buffer that held P(j-1): P.V(j-1) must be done.
+            ok = wait(&k_full[(j + 1) % KST], ((j + 1) / KST) & 1) &&
+                 (j < 1 || wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(j + 1);
+          }
+          ok = wait(&pv_ready[j % VST], (j / VST) & 1);
           if (!ok) break;
           tc_fence_after();
-          issue_s(j + 1);
+          issue_pv(j);
         }
-        ok = mbar_wait(&v_conv[j % VST], (j / VST) & 1, p.err, abort_flag, kErrTimeoutMma);
-        if (ok) ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, abort_flag, kErrTimeoutMma);
-        if (ok && j >= 1) ok = mbar_wait(ot_free, (j - 1) & 1, p.err, abort_flag, kErrTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(j);
       }
-    }
-  } else if (warp >= kWarpConv0) {
-    // ------------------------------------------------------ V converter --
-    const int t = static_cast<int>(threadIdx.x) - 32 * kWarpConv0;
-    int appended = 0;
-    for (int j = 0; j < nt; ++j) {
-      const int st = j % VST;
-      const uint32_t ph = (j / VST) & 1;
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], ph, p.err, abort_flag,
-                                                  kErrTimeoutConvert));
-      if (ok && attn_append_tile(p, j, qt)) {
-        ok = __all_sync(0xffffffffu, mbar_wait(v_stored, appended & 1, p.err, abort_flag,
-                                               kErrTimeoutConvert));
-        ++appended;
-      }
-      if (!ok) break;
-      uint4* tile = reinterpret_cast<uint4*>(smem + L::OFF_V + st * L::KV_BYTES);
-      float amax = 0.f;
-#pragma unroll 8
-      for (int i = t; i < L::KV_BYTES / 16; i += kConvThreads) {
-        uint4 w = tile[i];
-        w.x = attn_bf16x2_to_f16x2(w.x, amax);
-        w.y = attn_bf16x2_to_f16x2(w.y, amax);
-        w.z = attn_bf16x2_to_f16x2(w.z, amax);
-        w.w = attn_bf16x2_to_f16x2(w.w, amax);
-        tile[i] = w;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&v_conv[st]);
-      // Range check per warp share of the tile: a value of magnitude >= 2^16
-      // (inf included), or a share whose largest magnitude is below 2^-6,
-      // where values below 2^-17 would lose bits in fp16. (A NaN in V
-      // propagates to O as it does in fp32.)
-      const float wmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
-      if (lane == 0 && (!(wmax < 65536.f) || (wmax != 0.f && wmax < 0.015625f))) *needs_exact = 1;
     }
   } else if (warp < 8) {
     // ----------------------------------------------------------- softmax --
@@ -419,23 +441,34 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
         m_run = m_new;
       }
       const float neg_m = (m_run == -INFINITY) ? 0.f : kPScaleLog2 - m_run;
-      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      // pairs of columns on the packed fp32x2 pipe: one FMA and one add per pair
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t nm2 = f2_pack(neg_m, neg_m);
+      uint64_t ls2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         uint32_t phi[16], plo[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const int kk = q * 16 + k;
-          const float e0 = fast_exp2(fmaf(__uint_as_float(sv[2 * kk]), p.scale_log2, neg_m));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(sv[2 * kk + 1]), p.scale_log2, neg_m));
-          ls4[(2 * k) & 3] += e0;
-          ls4[(2 * k + 1) & 3] += e1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[2 * kk]), __uint_as_float(sv[2 * kk + 1])),
+                           sc2, nm2),
+                    x0, x1);
+          const float e0 = fast_exp2(x0);
+          const float e1 = fast_exp2(x1);
+          ls2[k & 1] = f2_add(ls2[k & 1], f2_pack(e0, e1));
           split_f16x2(e0, e1, phi[k], plo[k]);
         }
         tmem_st16(s_half + q * 16, phi);
         tmem_st16(s_half + 32 + q * 16, plo);
       }
-      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(ls2[0], a0, a1);
+        f2_unpack(ls2[1], b0, b1);
+        l_run += (a0 + b0) + (a1 + b1);
+      }
       if (hk == 0) {
         // hand the tile's O rescale factor to the correction warps
         const float tile_alpha =
@@ -448,82 +481,116 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[b]);
+      mbar_arrive(&pv_ready[j % VST]);
     }
     l_s[hk * BM + r] = l_run;
     mbar_arrive(l_ready);
   } else {
     // -------------------------------------------------------- correction --
+    setmaxnreg_inc<kRegsCorrection>();
     const int r = static_cast<int>(threadIdx.x) - 2 * BM;
     const int qi = qt * BM + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    bool ok = true;
-    for (int j = 0; j < nt; ++j) {
+    // V(j) is rewritten from bf16 to fp16 in place in shared memory (same
+    // layout, same swizzle) before P.V(j) reads it; every bf16 value in
+    // [2^-17, 65280] is exactly an fp16 value. Per tile j these warps convert
+    // V(j+1) and arrive on pv_ready(j+1) (V(j+1) in fp16, and Ot[(j+1)&1]
+    // drained of P.V(j-1) in the previous step), then fold P.V(j) from
+    // Ot[j&1] into the row's O, which lives in registers.
+    const int ct = static_cast<int>(threadIdx.x) - 2 * BM;  // 0..127
+    int appended = 0;
+    auto convert_v = [&](int j) -> bool {
+      const int st = j % VST;
+      bool okc = __all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / VST) & 1, p.err, abort_flag,
+                                                   kErrTimeoutConvert));
+      if (okc && attn_append_tile(p, j, qt)) {
+        okc = __all_sync(0xffffffffu, mbar_wait(v_stored, appended & 1, p.err, abort_flag,
+                                                kErrTimeoutConvert));
+        ++appended;
+      }
+      if (!okc) return false;
+      uint4* tile = reinterpret_cast<uint4*>(smem + L::OFF_V + st * L::KV_BYTES);
+      float amax = 0.f;
+#pragma unroll 4
+      for (int i = ct; i < L::KV_BYTES / 16; i += kConvThreads) {
+        uint4 w = tile[i];
+        w.x = attn_bf16x2_to_f16x2(w.x, amax);
+        w.y = attn_bf16x2_to_f16x2(w.y, amax);
+        w.z = attn_bf16x2_to_f16x2(w.z, amax);
+        w.w = attn_bf16x2_to_f16x2(w.w, amax);
+        tile[i] = w;
+      }
+      fence_proxy_async_smem();
+      // Range check per warp share of the tile: a value of magnitude >= 2^16
+      // (inf included), or a share whose largest magnitude is below 2^-6,
+      // where values below 2^-17 would lose bits in fp16. (A NaN in V
+      // propagates to O as it does in fp32.)
+      const float wmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+      if (lane == 0 && (!(wmax < 65536.f) || (wmax != 0.f && wmax < 0.015625f))) *needs_exact = 1;
+      return true;
+    };
+    float o[D];
+#pragma unroll
+    for (int k = 0; k < D; ++k) o[k] = 0.f;
+    // (a tile whose rows see no key has nt == 0 and still stores its zero rows)
+    bool ok = nt == 0 || convert_v(0);
+    if (ok && nt > 0) mbar_arrive(&pv_ready[0]);  // V(0) converted; Ot[0] holds nothing yet
+    for (int j = 0; j < nt && ok; ++j) {
       const int b = j & 1;
+      if (j + 1 < nt) {
+        if (!convert_v(j + 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive(&pv_ready[(j + 1) % VST]);
+      }
       ok = __all_sync(0xffffffffu, mbar_wait(&alpha_full[b], (j >> 1) & 1, p.err, abort_flag,
                                              kErrTimeoutSoftmax));
       if (!ok) break;
       const float a = alpha_s[b * BM + r];
       mbar_arrive(&alpha_empty[b]);
-      ok = __all_sync(0xffffffffu, mbar_wait(pv_done, j & 1, p.err, abort_flag,
+      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[b], (j >> 1) & 1, p.err, abort_flag,
                                              kErrTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t t[32];
-        tmem_ld32(lane_base + kColOt + c * 32, t);
-        if (j == 0) {
-          tmem_ld_wait();
-          tmem_st32(lane_base + kColO + c * 32, t);
-        } else {
-          uint32_t o[32];
-          tmem_ld32(lane_base + kColO + c * 32, o);
-          tmem_ld_wait();
+        tmem_ld32(lane_base + kColOt + b * 128 + c * 32, t);
+        tmem_ld_wait();
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            o[k] = __float_as_uint(fmaf(__uint_as_float(o[k]), a, __uint_as_float(t[k])));
-          tmem_st32(lane_base + kColO + c * 32, o);
-        }
+        for (int k = 0; k < 32; ++k) o[c * 32 + k] = fmaf(o[c * 32 + k], a, __uint_as_float(t[k]));
       }
-      tmem_st_wait();
+      // Ot[b] is read out: P.V(j+2) may overwrite it once pv_ready(j+2) says so
       tc_fence_before();
-      mbar_arrive(ot_free);
     }
     // ------------------------------------------------------- epilogue --
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(l_ready, 0, p.err, abort_flag,
                                                    kErrTimeoutSoftmax));
-    if (ok) {
+    if (ok && qi < p.S_q) {
       const float l = l_s[r] + l_s[BM + r];
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.O + (static_cast<long long>(bh) * p.S_q + qi) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        if (nt > 0) {
-          tmem_ld32(lane_base + kColO + c * 32, o);
-          tmem_ld_wait();
-        } else {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) o[k] = 0u;
-        }
-        if (qi < p.S_q) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
-            v.y = pack_bf16x2(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
-            v.z = pack_bf16x2(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
-            v.w = pack_bf16x2(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
-          }
-        }
+      for (int g = 0; g < D / 8; ++g) {
+        uint4 v;
+        v.x = pack_bf16x2(o[g * 8 + 0] * inv, o[g * 8 + 1] * inv);
+        v.y = pack_bf16x2(o[g * 8 + 2] * inv, o[g * 8 + 3] * inv);
+        v.z = pack_bf16x2(o[g * 8 + 4] * inv, o[g * 8 + 5] * inv);
+        v.w = pack_bf16x2(o[g * 8 + 6] * inv, o[g * 8 + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + g * 8) = v;
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  // Back to 128 registers everywhere for the common tail. Warpgroup 3 takes
+  // its registers back only after warpgroup 2 has returned them: were it to
+  // run ahead, it could take registers warpgroup 2's first increase waits for.
+  if (warp >= 8 && warp < 12) setmaxnreg_dec<128>();
+  __syncthreads();
+  if (warp >= kWarpProducer) setmaxnreg_inc<128>();
   if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

@@ -10,7 +10,7 @@
 // Structure (one CTA per SM, persistent over output tiles):
 //   warp 0   TMA producer: A tile 128x64 (K-major, 128B swizzle) and B tile
 //            64x256 as four 64x64 N-major boxes, into a STAGES-deep ring.
-//   warp 1   TMEM allocator + single-thread tcgen05.mma issuer
+//   warp 1   TMEM allocator + tcgen05.mma issuer (whole warp, one elected lane issues)
 //            (M=128, N=256, K=16 per instruction, 4 per stage).
 //   warps 2-9 epilogue (two per TMEM lane quarter, each owning half of the
 //            columns): tcgen05.ld 32 columns at a time from the finished
@@ -319,8 +319,15 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ------------------------------------------------------- MMA issuer --
+      // The whole warp runs the loop with warp-uniform values and one elected
+      // lane issues each MMA and commit (a single diverged thread issuing
+      // MMAs back to back is slower than the tensor core). Every wait is
+      // taken by all lanes and agreed with a vote, so the warp stays converged.
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, abort_flag, kErrTimeoutMma));
+      };
       constexpr uint32_t idesc = make_idesc_bf16(BM, BN, false, true);
       int stage = 0;
       uint32_t phase = 0;
@@ -329,9 +336,11 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       int slot = 0;
       uint32_t sphase = 0;
       for (;; ++local) {
-        if (!mbar_wait(&sched_full[slot], sphase, err, abort_flag, kErrTimeoutMma)) break;
+        if (!wait(&sched_full[slot], sphase)) break;
         const int t = sched_tile[slot];
-        mbar_arrive(&sched_empty[slot]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sched_empty[slot]);
+        __syncwarp();
         if (++slot == gemm::SCHED_DEPTH) {
           slot = 0;
           sphase ^= 1;
@@ -339,11 +348,11 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
         if (t < 0 || !ok) break;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err, abort_flag, kErrTimeoutMma)) break;
+        if (!wait(&tempty_bar[acc], acc_phase ^ 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, err, abort_flag, kErrTimeoutMma)) {
+          if (!wait(&full_bar[stage], phase)) {
             ok = false;
             break;
           }
@@ -354,15 +363,15 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = make_sw128_desc(b_addr + kk * 2048, B_BLOCK_BYTES, 1024);
-            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
+            tc_mma_f16_warp(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
           }
-          tc_commit(&empty_bar[stage]);
+          tc_commit_warp(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (ok) tc_commit(&tfull_bar[acc]);
+        if (ok) tc_commit_warp(&tfull_bar[acc]);
       }
     }
   } else {

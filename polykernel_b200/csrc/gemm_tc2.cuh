@@ -16,8 +16,8 @@
 //            half (two 64 x 64 N-major boxes); the loads' byte counts land on
 //            the leader CTA's full barrier (cta_group::2 loads, no multicast).
 //   warp 1   TMEM allocator in both CTAs (cta_group::2); in the leader, the
-//            single-thread MMA issuer. Its commits arrive on both CTAs'
-//            barriers (tcgen05.commit multicast).
+//            MMA issuer (whole warp, one elected lane issues). Its commits
+//            arrive on both CTAs' barriers (tcgen05.commit multicast).
 //   warps 2-9 epilogue in both CTAs: drain the CTA's own accumulator rows.
 // Tiles are statically assigned (cluster c takes tiles c, c + clusters, ...),
 // so the pair needs no shared schedule. Every mbarrier wait is bounded as in
@@ -75,23 +75,28 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// Issued by a whole converged warp; one elected lane runs the instruction.
 __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
 // Arrive once on `bar` (same offset) in both CTAs of the pair when the MMAs
-// issued so far have completed.
+// issued so far have completed. Issued by a whole converged warp; one elected
+// lane runs the instruction.
 __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
   const uint16_t mask = 0x3;
   asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(smem_u32(bar)), "h"(mask)
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(smem_u32(bar)), "h"(mask)
       : "memory");
 }
 
@@ -194,8 +199,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && cta == 0) {
+    if (cta == 0) {
       // ---------------------------------------------- MMA issuer (leader) --
+      // The whole warp runs the loop (warp-uniform values, every wait agreed
+      // by a vote); one elected lane issues each MMA and commit.
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, abort_flag, kErrTimeoutMma));
+      };
       constexpr uint32_t idesc = make_idesc_bf16(2 * BM, BN, false, true);
       int stage = 0;
       uint32_t phase = 0;
@@ -204,11 +214,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 
       for (int t = cluster; t < num_tiles && ok; t += clusters, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err, abort_flag, kErrTimeoutMma)) break;
+        if (!wait(&tempty_bar[acc], acc_phase ^ 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, err, abort_flag, kErrTimeoutMma)) {
+          if (!wait(&full_bar[stage], phase)) {
             ok = false;
             break;
           }

@@ -202,6 +202,24 @@ int variant_of(const tuning::Config& c) {
   return -1;
 }
 
+// The config used when neither a forced config nor a validated cache entry
+// applies: the CTA-pair kernel (256 x 256 tiles over two SMs, 6 stages) for
+// GEMMs with at least 512 rows, whose epilogue it supports; otherwise the
+// single-SM 128 x 256 kernel. Both produce bit-identical results.
+// PKB200_GEMM_PAIR=0 turns the pair default off.
+tuning::Config default_config(int epi, int M) {
+  static const bool pair_ok = [] {
+    const char* v = std::getenv("PKB200_GEMM_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  tuning::Config c{};
+  if (pair_ok && M >= 512 && epi != kEpiPeerStoreF32 && epi != kEpiQkvScatter) {
+    c.block_m = 2 * gemm::BM;
+    c.shared_memory_stages = 6;
+  }
+  return c;
+}
+
 // source: 0 default, 1 tuning cache, 2 forced.
 tuning::Config select_config(int epi, int M, int N, int K, int* source = nullptr) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -222,7 +240,7 @@ tuning::Config select_config(int epi, int M, int N, int K, int* source = nullptr
       }
     }
   }
-  return tuning::Config{};
+  return default_config(epi, M);
 }
 
 // -------------------------------------------------------------------- GEMM --
@@ -593,6 +611,15 @@ int launch_attention_tc_d(const bf16* Q, bf16* O, const KvSources& kv, int BH, i
   p.kv = kv;
   p.scale = scale;
   p.exact_ctas = exact_ctas;
+  {
+    // Heads per scheduling group: the K/V of the heads whose tiles run at the
+    // same time should stay in L2 (every query tile of a head reads all of
+    // its keys), so a group's K and V are held to about 32 MB.
+    const long long kv_bytes = static_cast<long long>(kv.n_a + kv.n_b) * D * 2 * 2;
+    long long g = kv_bytes > 0 ? (32LL << 20) / kv_bytes : BH;
+    if (g < 1) g = 1;
+    p.head_group = static_cast<int>(g < BH ? g : BH);
+  }
   dim3 grid(static_cast<unsigned>(p.num_qtiles) * static_cast<unsigned>(BH));
   attention_tc_kernel<D><<<grid, attn::NUM_THREADS, L::SMEM_BYTES, s>>>(mq, mka, mva, mkb, mvb,
                                                                         mks, mvs, p);

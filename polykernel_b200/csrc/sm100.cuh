@@ -70,6 +70,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Per-warpgroup register budget (all four warps of a warpgroup execute the
+// same instruction). inc waits until the registers are free; the callers'
+// budgets must add up to at most the launch's threads x registers.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Non-blocking test of the phase with the given parity (never suspends).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete. Returns false (after
 // recording `code` in *err and raising *abort) if the limit runs out or if
 // another role already aborted.
@@ -80,6 +105,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > limit) {
+      atomicCAS(err, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// mbar_wait that polls with the non-suspending test instead of try_wait: for
+// waits on the critical path of a latency-bound pipeline, where a suspended
+// waiter can resume well after the phase completes.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, int* err,
+                                               volatile int* abort_flag, int code,
+                                               long long limit = kSpinLimitCycles) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > limit) {
       atomicCAS(err, 0, code);
@@ -197,6 +241,42 @@ __device__ __forceinline__ void tc_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tm
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Warp-synchronous forms: the whole (converged) warp executes them with
+// warp-uniform operands and one lane, chosen by elect.sync, issues the
+// instruction. Issuing from a converged warp keeps the operands in the
+// uniform datapath; a single diverged thread issuing back-to-back MMAs was
+// measured to need ~190 cycles per instruction, against 64 (N=128) and 128
+// (N=256) cycles of tensor-core work.
+__device__ __forceinline__ void tc_mma_f16_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_tmem_a_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                       uint64_t b_desc, uint32_t idesc,
+                                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
       : "memory");
 }
 
