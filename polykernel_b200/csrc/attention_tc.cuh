@@ -324,6 +324,10 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
             atomicCAS(p.err, 0, kErrTimeoutProducer);
             *abort_flag = 1;
             ok = false;
+          } else {
+            // nothing to issue yet: sleep briefly instead of spinning, so the
+            // softmax warps sharing this SM sub-partition keep its issue slots
+            __nanosleep(64);
           }
         }
         bulk_wait_group0();
@@ -362,8 +366,7 @@ __global__ void __launch_bounds__(attn::NUM_THREADS, 1)
         };
         // every wait is taken by the whole warp, so the warp stays converged
         auto wait = [&](uint64_t* bar, uint32_t parity) {
-          return __all_sync(0xffffffffu,
-                            mbar_wait_poll(bar, parity, p.err, abort_flag, kErrTimeoutMma));
+          return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, abort_flag, kErrTimeoutMma));
         };
         bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
         if (ok) {
