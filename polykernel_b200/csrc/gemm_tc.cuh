@@ -274,8 +274,14 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
   const uint32_t tmem_base = *tmem_base_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
+    {
       // ---------------------------------------------------------- producer --
+      // The whole warp runs the loop (warp-uniform values, waits agreed by a
+      // vote); one elected lane issues each TMA load and barrier arrival.
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu,
+                          mbar_wait(bar, parity, err, abort_flag, kErrTimeoutProducer));
+      };
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -286,31 +292,38 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       // SMs, then take fewer tiles), else by stride.
       int t = blockIdx.x;
       while (ok) {
-        if (!mbar_wait(&sched_empty[slot], sphase ^ 1, err, abort_flag, kErrTimeoutProducer)) break;
-        sched_tile[slot] = t < num_tiles ? t : -1;
-        mbar_arrive(&sched_full[slot]);
+        if (!wait(&sched_empty[slot], sphase ^ 1)) break;
+        if (lane == 0) {
+          sched_tile[slot] = t < num_tiles ? t : -1;
+          mbar_arrive(&sched_full[slot]);
+        }
+        __syncwarp();
         if (++slot == gemm::SCHED_DEPTH) {
           slot = 0;
           sphase ^= 1;
         }
         if (t >= num_tiles) break;
-        const int next = tile_counter ? static_cast<int>(gridDim.x) + atomicAdd(tile_counter, 1)
-                                      : t + static_cast<int>(gridDim.x);
+        int next = 0;
+        if (lane == 0)
+          next = tile_counter ? static_cast<int>(gridDim.x) + atomicAdd(tile_counter, 1)
+                              : t + static_cast<int>(gridDim.x);
+        next = __shfl_sync(0xffffffffu, next, 0);
         int mb, nb;
         tile_coords(t, tiles_m, tiles_n, group_m, mb, nb);
         t = next;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag, kErrTimeoutProducer)) {
+          if (!wait(&empty_bar[stage], phase ^ 1)) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-          tma_load_2d(sa, &map_a, &full_bar[stage], kb * BK, mb * BM);
+          mbar_arrive_expect_tx_warp(&full_bar[stage], STAGE_BYTES);
+          tma_load_2d_warp(sa, &map_a, &full_bar[stage], kb * BK, mb * BM);
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(sb + j * B_BLOCK_BYTES, &map_b, &full_bar[stage], nb * BN + j * 64, kb * BK);
+            tma_load_2d_warp(sb + j * B_BLOCK_BYTES, &map_b, &full_bar[stage], nb * BN + j * 64,
+                             kb * BK);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;

@@ -66,11 +66,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 
 // TMA tile load whose completion (byte count) lands on the pair leader's
 // barrier: `bar_leader` is the barrier's address in the leader CTA.
+// Issued by a whole converged warp; one elected lane runs the instruction.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
                                                  uint32_t bar_leader, int c0, int c1) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];\n\t}" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_leader), "r"(c0), "r"(c1)
       : "memory");
 }
@@ -169,8 +172,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
+    {
       // ---------------------------------------------------------- producer --
+      // whole warp, warp-uniform values, one elected lane issues
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -178,14 +182,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::NUM_THREADS, 
         int mb, nb;
         tile_coords(t, tiles_m, tiles_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag, kErrTimeoutProducer)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&empty_bar[stage], phase ^ 1, err, abort_flag,
+                                                 kErrTimeoutProducer))) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           const uint32_t bar = map_to_rank(smem_u32(&full_bar[stage]), 0);
-          if (cta == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
+          if (cta == 0) mbar_arrive_expect_tx_warp(&full_bar[stage], 2 * STAGE_BYTES);
           tma_load_2d_pair(sa, &map_a, bar, kb * BK, mb * 2 * BM + static_cast<int>(cta) * BM);
 #pragma unroll
           for (int j = 0; j < 2; ++j)
