@@ -193,7 +193,68 @@ constexpr int smem_bytes_peer(int bn, int stages) {
   return stages * stage_bytes(bn) + 1024 /*barriers*/ + kPeerStageBytes + 1024 /*align*/;
 }
 constexpr int kMaxSmem = 232448;                    // 227 KB per CTA on sm_100
+// Narrow weights (B as int8 / fp8 codes in HBM): BT selects the code type.
+// Shared memory then holds three rings: A tiles and the weights' 1-byte codes
+// (STAGES deep, one TMA barrier per slot, deep enough to cover load latency),
+// and the bf16 B tiles the MMA reads (kBf16Stages deep), which kConvWarps
+// extra warps fill by expanding the codes.
+constexpr int kBtBf16 = 0, kBtInt8 = 1, kBtE4M3 = 2, kBtE5M2 = 3;
+constexpr int kConvWarps = 8;
+constexpr int kBf16Stages = 2;
+constexpr int raw_bytes(int bn) { return BK * bn; }
+constexpr int threads_for(int bt) { return NUM_THREADS + (bt ? 32 * kConvWarps : 0); }
+constexpr int smem_bytes_narrow(int bn, int stages) {
+  return stages * (a_bytes() + raw_bytes(bn)) + kBf16Stages * b_bytes(bn) + 1024 + 512;
+}
 }  // namespace gemm
+
+// Four int8 codes -> four bf16 (exact: |q| <= 128 needs 8 bits). The byte plus
+// 128 is placed in the low mantissa bits of 2^23, and 2^23 + 128 subtracted.
+__device__ __forceinline__ void int8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  constexpr float kMagic = 8388736.0f;  // 2^23 + 128
+  const float f0 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440)) - kMagic;
+  const float f1 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7441)) - kMagic;
+  const float f2 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7442)) - kMagic;
+  const float f3 = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7443)) - kMagic;
+  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+}
+
+// Two fp8 codes (low byte first) -> two bf16, through the hardware fp8 -> fp16
+// conversion (exact) and fp16 -> fp32 -> bf16 (exact: an fp8 value has at most
+// 4 significant bits and lies in bf16's exponent range).
+template <int BT>
+__device__ __forceinline__ uint32_t fp8x2_to_bf16x2(uint32_t codes16) {
+  uint32_t h;
+  const uint16_t c = static_cast<uint16_t>(codes16);
+  if constexpr (BT == gemm::kBtE4M3)
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(c));
+  else
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h) : "h"(c));
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  return pack_bf16x2(f.x, f.y);
+}
+
+// 16 codes -> 16 bf16 (two 16-byte chunks).
+template <int BT>
+__device__ __forceinline__ void codes16_to_bf16(const uint4 w, uint4& o0, uint4& o1) {
+  if constexpr (BT == gemm::kBtInt8) {
+    int8x4_to_bf16x4(w.x, o0.x, o0.y);
+    int8x4_to_bf16x4(w.y, o0.z, o0.w);
+    int8x4_to_bf16x4(w.z, o1.x, o1.y);
+    int8x4_to_bf16x4(w.w, o1.z, o1.w);
+  } else {
+    o0.x = fp8x2_to_bf16x2<BT>(w.x & 0xFFFFu);
+    o0.y = fp8x2_to_bf16x2<BT>(w.x >> 16);
+    o0.z = fp8x2_to_bf16x2<BT>(w.y & 0xFFFFu);
+    o0.w = fp8x2_to_bf16x2<BT>(w.y >> 16);
+    o1.x = fp8x2_to_bf16x2<BT>(w.z & 0xFFFFu);
+    o1.y = fp8x2_to_bf16x2<BT>(w.z >> 16);
+    o1.z = fp8x2_to_bf16x2<BT>(w.w & 0xFFFFu);
+    o1.w = fp8x2_to_bf16x2<BT>(w.w >> 16);
+  }
+}
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& mb,
                                             int& nb) {
@@ -206,8 +267,8 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   nb = local / gm;
 }
 
-template <int EPI, int BN, int STAGES>
-__global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
+template <int EPI, int BN, int STAGES, int BT = gemm::kBtBf16>
+__global__ void __launch_bounds__(gemm::threads_for(BT), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, void* __restrict__ C, long long ldc,
                    int M, int N, int K, EpilogueArgs ea, int* err,
@@ -221,12 +282,23 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
   constexpr int TMEM_COLS = gemm::tmem_cols(BN);
   static_assert(BN == 128 || BN == 256, "tile width");
   static_assert((EPI == kEpiPeerStoreF32 ? gemm::smem_bytes_peer(BN, STAGES)
-                                         : gemm::smem_bytes(BN, STAGES)) <= gemm::kMaxSmem,
+                 : BT                   ? gemm::smem_bytes_narrow(BN, STAGES)
+                                        : gemm::smem_bytes(BN, STAGES)) <= gemm::kMaxSmem,
                 "pipeline does not fit");
+  static_assert(BT == gemm::kBtBf16 || (BN == 256 && EPI != kEpiPeerStoreF32),
+                "narrow weights: 256-wide tiles, no peer-store epilogue");
+  constexpr int BST = gemm::kBf16Stages;
+  constexpr int RAW_BYTES = gemm::raw_bytes(BN);
+  constexpr int B_BYTES = gemm::b_bytes(BN);
+  constexpr int CONV_WARPS = BT ? gemm::kConvWarps : 0;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bf16 B: STAGES slots of [A | B]. Narrow B: [A ring][code ring][bf16 B ring].
+  uint8_t* raw_ring = smem + STAGES * gemm::a_bytes();
+  uint8_t* b_ring = raw_ring + STAGES * RAW_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(
+      BT ? b_ring + BST * B_BYTES : smem + STAGES * STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -236,6 +308,9 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
   volatile int* sched_tile = reinterpret_cast<volatile int*>(sched_empty + gemm::SCHED_DEPTH);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(sched_tile) + gemm::SCHED_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  // narrow B: bf16 B ring barriers (after the tile ring; 8-byte aligned)
+  uint64_t* bfull_bar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);
+  uint64_t* bempty_bar = bfull_bar + gemm::kBf16Stages;
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -247,7 +322,8 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      // freed by the MMA's commit (+ each converter warp, done with the codes)
+      mbar_init(&empty_bar[s], 1 + CONV_WARPS);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
@@ -255,7 +331,14 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     }
     for (int i = 0; i < gemm::SCHED_DEPTH; ++i) {
       mbar_init(&sched_full[i], 1);
-      mbar_init(&sched_empty[i], 1 + EPI_THREADS / 32);  // MMA issuer + one lane per epilogue warp
+      // MMA issuer + one lane per epilogue warp (+ one per converter warp)
+      mbar_init(&sched_empty[i], 1 + EPI_THREADS / 32 + CONV_WARPS);
+    }
+    if (BT) {
+      for (int i = 0; i < BST; ++i) {
+        mbar_init(&bfull_bar[i], CONV_WARPS);
+        mbar_init(&bempty_bar[i], 1);
+      }
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -318,12 +401,25 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          mbar_arrive_expect_tx_warp(&full_bar[stage], STAGE_BYTES);
-          tma_load_2d_warp(sa, &map_a, &full_bar[stage], kb * BK, mb * BM);
+          if constexpr (BT == gemm::kBtBf16) {
+            mbar_arrive_expect_tx_warp(&full_bar[stage], STAGE_BYTES);
+            tma_load_2d_warp(sa, &map_a, &full_bar[stage], kb * BK, mb * BM);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d_warp(sb + j * B_BLOCK_BYTES, &map_b, &full_bar[stage], nb * BN + j * 64,
-                             kb * BK);
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d_warp(sb + j * B_BLOCK_BYTES, &map_b, &full_bar[stage],
+                               nb * BN + j * 64, kb * BK);
+          } else {
+            // A and the B codes of this k-block, both on the slot's barrier;
+            // the converter warps expand the codes into the bf16 B ring
+            uint8_t* ra = smem + stage * gemm::a_bytes();
+            uint8_t* sr = raw_ring + stage * RAW_BYTES;
+            mbar_arrive_expect_tx_warp(&full_bar[stage], gemm::a_bytes() + RAW_BYTES);
+            tma_load_2d_warp(ra, &map_a, &full_bar[stage], kb * BK, mb * BM);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_warp(sr + j * (BK * 128), &map_b, &full_bar[stage], nb * BN + j * 128,
+                               kb * BK);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -344,6 +440,8 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
       constexpr uint32_t idesc = make_idesc_bf16(BM, BN, false, true);
       int stage = 0;
       uint32_t phase = 0;
+      int bstage = 0;  // narrow B: bf16 B ring
+      uint32_t bphase = 0;
       int local = 0;
       bool ok = true;
       int slot = 0;
@@ -365,13 +463,15 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!wait(&full_bar[stage], phase)) {
+          if (!wait(&full_bar[stage], phase) ||
+              (BT != gemm::kBtBf16 && !wait(&bfull_bar[bstage], bphase))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_BYTES;
+          const uint32_t a_addr = BT ? smem_u32(smem + stage * A_BYTES)
+                                     : smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = BT ? smem_u32(b_ring + bstage * B_BYTES) : a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
@@ -383,8 +483,78 @@ __global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
+          if constexpr (BT != gemm::kBtBf16) {
+            tc_commit_warp(&bempty_bar[bstage]);
+            if (++bstage == BST) {
+              bstage = 0;
+              bphase ^= 1;
+            }
+          }
         }
         if (ok) tc_commit_warp(&tfull_bar[acc]);
+      }
+    }
+  } else if (BT != gemm::kBtBf16 && warp >= 2 + EPI_THREADS / 32) {
+    // --------------------------------------------------------- converters --
+    // Each k-block's codes (BK rows x BN codes, two 128-byte swizzled boxes)
+    // are expanded to bf16 into the next bf16 B slot (four 128-byte swizzled
+    // boxes of 64 columns), in the order the producer loaded them; the tile
+    // ring only tells how many k-blocks follow.
+    const int ct = static_cast<int>(threadIdx.x) - 32 * (2 + EPI_THREADS / 32);
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, abort_flag, kErrTimeoutEpilogue));
+    };
+    int stage = 0, bstage = 0, slot = 0;
+    uint32_t phase = 0, bphase = 0, sphase = 0;
+    bool ok = true;
+    while (ok) {
+      if (!wait(&sched_full[slot], sphase)) break;
+      const int t = sched_tile[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sched_empty[slot]);
+      __syncwarp();
+      if (++slot == gemm::SCHED_DEPTH) {
+        slot = 0;
+        sphase ^= 1;
+      }
+      if (t < 0) break;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        // the codes have landed, and the MMA is done with this bf16 B slot
+        if (!wait(&full_bar[stage], phase) || !wait(&bempty_bar[bstage], bphase ^ 1)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* sr = raw_ring + stage * RAW_BYTES;
+        uint8_t* sb = b_ring + bstage * B_BYTES;
+#pragma unroll 2
+        for (int u = ct; u < RAW_BYTES / 16; u += 32 * CONV_WARPS) {
+          const int box = u >> 9;           // 128-code box (512 chunks each)
+          const int k = (u >> 3) & 63;      // row (k)
+          const int c8 = u & 7;             // 16-code chunk within the row
+          const uint4 w =
+              *reinterpret_cast<const uint4*>(sr + box * (BK * 128) + k * 128 + ((c8 ^ (k & 7)) << 4));
+          uint4 o0, o1;
+          codes16_to_bf16<BT>(w, o0, o1);
+          uint8_t* row = sb + (2 * box + (c8 >> 2)) * B_BLOCK_BYTES + k * 128;
+          const int cb = 2 * (c8 & 3);
+          *reinterpret_cast<uint4*>(row + ((cb ^ (k & 7)) << 4)) = o0;
+          *reinterpret_cast<uint4*>(row + (((cb + 1) ^ (k & 7)) << 4)) = o1;
+        }
+        fence_proxy_async_smem();  // the MMA reads the slot through the async proxy
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bfull_bar[bstage]);
+          mbar_arrive(&empty_bar[stage]);  // done with the codes
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++bstage == BST) {
+          bstage = 0;
+          bphase ^= 1;
+        }
       }
     }
   } else {

@@ -462,6 +462,78 @@ int run_gemm(const bf16* A, const bf16* B, void* C, int M, int N, int K, const E
   return launch_gemm_simt<EPI, bf16>(A, B, C, M, N, K, ea, s);
 }
 
+// Tensor-core GEMM whose B operand is stored as 1-byte codes (int8 or fp8):
+// the kernel TMA-loads the codes and expands them to bf16 in shared memory
+// (gemm_tc.cuh, converter warps), so no bf16 copy of the weights is written.
+// Same K order and epilogue as run_gemm on the expanded weights: bit-identical.
+// Opt-in (PKB200_NARROW_GEMM=1): at config-4 shapes the converter warps'
+// instructions (~2 per weight per 128-row tile) slow the GEMM more than the
+// separate expansion pass costs (fp8 GEMM1 0.62 ms against 0.41 ms with the
+// pass; with the conversion work removed the same pipeline runs 0.34 ms).
+// cudaErrorNotSupported when not enabled or for shapes it cannot take (the
+// caller then expands into the workspace).
+bool narrow_gemm_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("PKB200_NARROW_GEMM");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+template <int EPI, int BT>
+int run_gemm_narrow(const bf16* A, const void* Bq, void* C, int M, int N, int K,
+                    const EpilogueArgs& ea, cudaStream_t s) {
+  constexpr int STAGES = 5;  // A and code slots; two bf16 B slots besides
+  constexpr int BN = 256;
+  if (M < 0 || N < 0 || K < 0) return cudaErrorInvalidValue;
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (!narrow_gemm_enabled()) return cudaErrorNotSupported;
+  if (!(K > 0 && (K % 8) == 0 && (N % 16) == 0 && aligned16(A) && aligned16(Bq) && aligned16(C) &&
+        (!ea.bias || aligned16(ea.bias)) && (!ea.resid || aligned16(ea.resid)) &&
+        (!ea.col_scale || aligned16(ea.col_scale)) && encode_fn() != nullptr))
+    return cudaErrorNotSupported;
+  DeviceInfo* di = nullptr;
+  int e = current_device_info(&di);
+  if (e) return e;
+  CUtensorMap ma, mb;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t str[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {64, gemm::BM};
+    if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, dims, str, box))
+      return cudaErrorInvalidValue;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K)};
+    const cuuint64_t str[1] = {static_cast<cuuint64_t>(N)};
+    const cuuint32_t box[2] = {128, gemm::BK};
+    if (!make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, Bq, dims, str, box))
+      return cudaErrorInvalidValue;
+  }
+  constexpr int smem = gemm::smem_bytes_narrow(BN, STAGES);
+  if (const int e2 = ensure_smem_attr(
+          reinterpret_cast<const void*>(gemm_tc_kernel<EPI, BN, STAGES, BT>), smem))
+    return e2;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + BN - 1) / BN);
+  int ctas = di->sms;
+  const int cap = g_gemm_max_ctas.load();
+  if (cap > 0 && cap < ctas) ctas = cap;
+  const int grid = tiles < ctas ? tiles : ctas;
+  static const PeerMaps kNoPeers{};
+  int* counter = nullptr;
+  if (g_gemm_dynamic.load() && tiles > grid) {
+    if ((e = next_tile_counter(dev, &counter))) return e;
+    if ((e = cudaMemsetAsync(counter, 0, sizeof(int), s))) return e;
+  }
+  gemm_tc_kernel<EPI, BN, STAGES, BT><<<grid, gemm::threads_for(BT), smem, s>>>(
+      ma, mb, C, static_cast<long long>(N), M, N, K, ea, di->err, kNoPeers, counter,
+      group_tiles(gemm::BM));
+  g_counters[kCntGemmTc]++;
+  return cudaGetLastError();
+}
+
 // int8 -> bf16 weight expansion (exact: |q| <= 127 fits bf16's 8-bit significand).
 __global__ void int8_to_bf16_kernel(const int8_t* __restrict__ q, bf16* __restrict__ out,
                                     long long n) {
@@ -1313,6 +1385,8 @@ int pkb200_matmul_int8(const void* A, const int8_t* Wq, const float* scale, void
   const bool tc_shape = K > 0 && (K % 8) == 0 && (N % 8) == 0 && aligned16(A) && aligned16(C) &&
                         aligned16(Wq) && aligned16(scale);
   if (!tc_shape) return launch_gemm_simt<kEpiColScale, int8_t>(cb(A), Wq, C, M, N, K, ea, S(stream));
+  e = run_gemm_narrow<kEpiColScale, gemm::kBtInt8>(cb(A), Wq, C, M, N, K, ea, S(stream));
+  if (e != cudaErrorNotSupported) return e;
   void* ws = nullptr;
   e = library_workspace(align_up(static_cast<size_t>(K) * N * 2), S(stream), &ws);
   if (e) return e;
@@ -1350,6 +1424,13 @@ static int matmul_fp8_impl(int kind, const void* A, const void* W, void* C, int 
   DeviceInfo* di = nullptr;
   int e = current_device_info(&di);
   if (e) return e;
+  if (kind == 1) {
+    // stored fp8 codes: expanded to bf16 inside the GEMM
+    e = fmt == kFp8E4M3
+            ? run_gemm_narrow<kEpiPlain, gemm::kBtE4M3>(cb(A), W, C, M, N, K, EpilogueArgs{}, S(stream))
+            : run_gemm_narrow<kEpiPlain, gemm::kBtE5M2>(cb(A), W, C, M, N, K, EpilogueArgs{}, S(stream));
+    if (e != cudaErrorNotSupported) return e;
+  }
   void* ws = nullptr;
   const long long kn = static_cast<long long>(K) * N;
   e = library_workspace(align_up(static_cast<size_t>(kn > 128 ? kn : 128) * 2), S(stream), &ws);
@@ -1473,21 +1554,28 @@ int pkb200_mlp_block_int8(const void* X, const void* gamma, const int8_t* W1q,
   if (e) return e;
   // GEMM1: int8 matmul with the per-channel scale, bias and GELU in its
   // epilogue (matmul_int8 -> bias -> gelu, each rounded to bf16 as the golden).
-  e = run_int8_expand(W1q, wexp, static_cast<long long>(d) * ffn, S(stream), di);
-  if (e) return e;
+  // The int8 codes are expanded to bf16 inside the GEMM (run_gemm_narrow);
+  // shapes it cannot take expand into the workspace first.
   EpilogueArgs ea{};
   ea.col_scale = s1;
   ea.bias = cb(b1);
-  e = run_gemm<kEpiScaleBiasGelu>(xn, wexp, h, M, ffn, d, ea, S(stream));
+  e = run_gemm_narrow<kEpiScaleBiasGelu, gemm::kBtInt8>(xn, W1q, h, M, ffn, d, ea, S(stream));
+  if (e == cudaErrorNotSupported) {
+    e = run_int8_expand(W1q, wexp, static_cast<long long>(d) * ffn, S(stream), di);
+    if (e) return e;
+    e = run_gemm<kEpiScaleBiasGelu>(xn, wexp, h, M, ffn, d, ea, S(stream));
+  }
   if (e) return e;
   // GEMM2: scale, bias and residual in its epilogue.
-  e = run_int8_expand(W2q, wexp, static_cast<long long>(ffn) * d, S(stream), di);
-  if (e) return e;
   EpilogueArgs eb{};
   eb.col_scale = s2;
   eb.bias = cb(b2);
   eb.resid = cb(X);
   eb.ld_resid = d;
+  e = run_gemm_narrow<kEpiScaleBiasResid, gemm::kBtInt8>(h, W2q, Y, M, d, ffn, eb, S(stream));
+  if (e != cudaErrorNotSupported) return e;
+  e = run_int8_expand(W2q, wexp, static_cast<long long>(ffn) * d, S(stream), di);
+  if (e) return e;
   return run_gemm<kEpiScaleBiasResid>(h, wexp, Y, M, d, ffn, eb, S(stream));
 }
 

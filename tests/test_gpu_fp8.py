@@ -124,3 +124,46 @@ def test_fp8_rejects_bad_arguments(pk):
         pk.ops.matmul_fp8(a, w)  # bf16 weights are not fp8 codes
     assert pk.lib().pkb200_matmul_fp8_sim(a.data_ptr(), w.data_ptr(), a.data_ptr(), 4, 8, 8, 7,
                                           None) != 0
+
+
+_NARROW_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+import polykernel_b200 as pk
+from oracle import golden_np as O
+from tests.helpers import bits_from_t, t_from_bits
+kind = sys.argv[2]
+rng = np.random.default_rng(31)
+M, K, N = 640, 1536, 1024
+A = t_from_bits(O.to_bits(rng.standard_normal((M, K)).astype(np.float32)))
+if kind == "int8":
+    q = torch.from_numpy(rng.integers(-128, 128, size=(K, N + 8), dtype=np.int8)).cuda()
+    sc = torch.from_numpy((rng.random(N + 8) * 0.02 + 0.001).astype(np.float32)).cuda()
+    wide = pk.ops.matmul_int8(A, q, sc)
+    narrow = pk.ops.matmul_int8(A, q[:, :N].contiguous(), sc[:N].contiguous())
+else:
+    W = t_from_bits(O.to_bits((rng.standard_normal((K, N + 8)) / 32).astype(np.float32)))
+    wq = pk.ops.quantize_fp8(W, kind)
+    wide = pk.ops.matmul_fp8(A, wq)
+    narrow = pk.ops.matmul_fp8(A, wq[:, :N].contiguous())
+assert np.array_equal(bits_from_t(narrow), bits_from_t(wide[:, :N].contiguous()))
+assert pk.device_error() == 0
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("kind", ["int8", "e4m3", "e5m2"])
+def test_narrow_weights_in_gemm_match_expanded_path(kind):
+    """With PKB200_NARROW_GEMM=1, weights stored as 1-byte codes are expanded
+    inside the tensor-core GEMM when N is a multiple of 16; other widths expand
+    into a bf16 workspace first. Both give the same bits: the same weights
+    padded to a width of N + 8 (expanded path) agree with width N (in-GEMM path)
+    column for column. Run in a child process, since the switch is read once."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PKB200_NARROW_GEMM="1")
+    r = subprocess.run([sys.executable, "-c", _NARROW_SCRIPT, root, kind], env=env, cwd=root,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
